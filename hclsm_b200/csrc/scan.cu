@@ -1,0 +1,897 @@
+// Level-0 selective SSM scan for B200 (sm_100a): forward and backward.
+//
+// Reference semantics: hclsm/kernels/ssm_scan_kernel.py
+//   sequential_ssm_scan :42-86 (clamp=1), parallel_ssm_scan_pytorch :168-218 and
+//   _ssm_scan_fwd_kernel :227-290 (clamp=0), _TritonSSMScan.backward :321-377.
+//   Recurrence per (sequence, channel d, state s):
+//     h_t = exp(dt_t * A_ds) * h_{t-1} + (dt_t * B_ts) * x_t ,  y_t = sum_s h_t * C_ts
+//   with A = -exp(A_log) (clamp=0) or A = -clamp(exp(A_log), 1e-6, 1), dt clamped to
+//   [1e-3, 1] (clamp=1).  With clamp=1, dt*A lies in [-1, 0), so the reference's
+//   clamp of dt*A to [-20, 0] (:77) never binds and is not evaluated here.
+//
+// Layout: x, dt, z, y and their gradients are (nseq, L, d_inner) row-major, so a
+// warp's 32 lanes own 32 consecutive channels and read one contiguous row segment
+// per timestep.  B and C (nseq, L, d_state) are shared by every channel of a
+// sequence and are broadcast from shared memory.  Every lane keeps its d_state
+// fp32 states in registers; time runs sequentially inside the thread.
+//
+// Backward: the reverse sweep needs h_{t-1} at every step.  The kernel runs a
+// forward sweep that leaves a checkpoint of h every K steps in shared memory, and
+// for each K-step chunk (last to first) recomputes the chunk and parks h_t and
+// exp(dt*A) for the K steps in tensor memory (TMEM: 128 lanes x 512 columns x 4 B,
+// one lane per thread), then walks the chunk backwards.  Cross-channel sums (dB,
+// dC) are reduced inside each warp by a halving butterfly and across warps in a
+// per-chunk shared slab.  dA_log / dD are reduced over sequences by a separate,
+// deterministic kernel.
+#include <algorithm>
+#include <cmath>
+#include <vector>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace hclsm {
+namespace scan {
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+constexpr int kFwdThreads = 128;
+constexpr int kFwdTC = 64;  // timesteps of B/C staged per shared-memory pass
+
+struct FwdParams {
+  const void* x;
+  const void* dt;
+  const float* A_log;
+  const void* B;
+  const void* C;
+  const float* Dp;
+  const void* z;
+  void* y;
+  int64_t nseq;
+  int L, D, S;
+};
+
+template <typename T, int SP, int CPT, bool CLAMP>
+__global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdParams p) {
+  __shared__ float sB[kFwdTC][SP];
+  __shared__ float sC[kFwdTC][SP];
+
+  const int64_t b = blockIdx.y;
+  const int D = p.D, S = p.S, L = p.L;
+  const int d0 = (blockIdx.x * kFwdThreads + threadIdx.x) * CPT;
+  const T* __restrict__ x = static_cast<const T*>(p.x);
+  const T* __restrict__ dt = static_cast<const T*>(p.dt);
+  const T* __restrict__ Bm = static_cast<const T*>(p.B);
+  const T* __restrict__ Cm = static_cast<const T*>(p.C);
+  const T* __restrict__ z = static_cast<const T*>(p.z);
+  T* __restrict__ y = static_cast<T*>(p.y);
+
+  bool act[CPT];
+  float A2[CPT][SP], h[CPT][SP], Dv[CPT];
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    act[c] = d0 + c < D;
+    Dv[c] = (p.Dp && act[c]) ? p.Dp[d0 + c] : 0.0f;
+#pragma unroll
+    for (int s = 0; s < SP; ++s) {
+      float a2 = 0.0f;
+      if (act[c] && s < S) {
+        float e = ex2(p.A_log[(int64_t)(d0 + c) * S + s] * kLog2e);
+        if (CLAMP) e = fminf(fmaxf(e, 1e-6f), 1.0f);
+        a2 = -e * kLog2e;
+      }
+      A2[c][s] = a2;
+      h[c][s] = 0.0f;
+    }
+  }
+  const bool pair = (CPT == 2) && act[0] && act[CPT - 1];
+
+  for (int t0 = 0; t0 < L; t0 += kFwdTC) {
+    const int tc = min(kFwdTC, L - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < tc * SP; i += kFwdThreads) {
+      const int tt = i / SP, s = i % SP;
+      const int64_t row = (b * L + t0 + tt) * S;
+      sB[tt][s] = s < S ? io<T>::ld(Bm + row + s) : 0.0f;
+      sC[tt][s] = s < S ? io<T>::ld(Cm + row + s) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int tt = 0; tt < tc; ++tt) {
+      const int64_t idx = (b * L + t0 + tt) * D + d0;
+      float xv[CPT], dv[CPT];
+      if (pair) {
+        float2 a = io<T>::ld2(x + idx), q = io<T>::ld2(dt + idx);
+        xv[0] = a.x; xv[CPT - 1] = a.y; dv[0] = q.x; dv[CPT - 1] = q.y;
+      } else {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          xv[c] = act[c] ? io<T>::ld(x + idx + c) : 0.0f;
+          dv[c] = act[c] ? io<T>::ld(dt + idx + c) : 0.0f;
+        }
+      }
+      float dtx[CPT], yv[CPT];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        if (CLAMP) dv[c] = fminf(fmaxf(dv[c], 1e-3f), 1.0f);
+        dtx[c] = dv[c] * xv[c];
+        yv[c] = 0.0f;
+      }
+#pragma unroll
+      for (int s = 0; s < SP; ++s) {
+        const float bs = sB[tt][s], cs = sC[tt][s];
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          const float dA = ex2(dv[c] * A2[c][s]);
+          h[c][s] = fmaf(dA, h[c][s], dtx[c] * bs);
+          yv[c] = fmaf(h[c][s], cs, yv[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        yv[c] = fmaf(Dv[c], xv[c], yv[c]);
+      }
+      if (z) {
+        float zv[CPT];
+        if (pair) {
+          float2 a = io<T>::ld2(z + idx);
+          zv[0] = a.x; zv[CPT - 1] = a.y;
+        } else {
+#pragma unroll
+          for (int c = 0; c < CPT; ++c) zv[c] = act[c] ? io<T>::ld(z + idx + c) : 0.0f;
+        }
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) yv[c] *= zv[c] * sigmoid(zv[c]);
+      }
+      if (pair) {
+        io<T>::st2(y + idx, yv[0], yv[CPT - 1]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c)
+          if (act[c]) io<T>::st(y + idx + c, yv[c]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+constexpr int kBwdThreads = 128;  // one thread per TMEM lane
+constexpr int kTmemCols = 512;
+
+template <typename T, int SP>
+struct BwdCfg {
+  static constexpr int K = (256 / SP) < 32 ? (256 / SP) : 32;  // history steps per chunk
+  static constexpr int NV = 2 * SP;                             // dB and dC values per step
+  static constexpr int NSTAGE = sizeof(T) == 2 ? 2 : 1;
+  static constexpr int NTEN = 4;  // x, dt, dy, z tiles
+  static constexpr size_t tile_elems = (size_t)K * kBwdThreads;
+  static constexpr size_t stage_bytes = NTEN * tile_elems * sizeof(T);
+};
+
+struct BwdParams {
+  const void* x;
+  const void* dt;
+  const float* A_log;
+  const void* B;
+  const void* C;
+  const float* Dp;
+  const void* z;
+  const void* dy;
+  void* dx;
+  void* ddt;
+  void* dz;
+  float* dAlog_part;  // (nseq, D, S): per-sequence partial of dA_log
+  float* dD_part;     // (nseq, D)
+  float* dBC_ws;      // (nsplit, nseq, L, 2*SP) fp32 accumulators of dB | dC
+  int64_t nseq;
+  int L, D, S;
+  int nck;             // number of K-step chunks
+  int groups;          // number of 128-channel groups
+  int groups_per_cta;  // contiguous groups handled by one CTA
+  int nsplit;
+  int* err;
+};
+
+// Host and device agree on this shared-memory layout.
+template <typename T, int SP>
+struct BwdSmem {
+  using Cfg = BwdCfg<T, SP>;
+  __host__ __device__ static size_t tiles_off() { return 0; }
+  __host__ __device__ static size_t bc_off() { return Cfg::NSTAGE * Cfg::stage_bytes; }
+  __host__ __device__ static size_t slab_off(int L) { return bc_off() + (size_t)L * SP * 2 * sizeof(float); }
+  __host__ __device__ static size_t ckpt_off(int L) { return slab_off(L) + 4 * (size_t)Cfg::K * Cfg::NV * sizeof(float); }
+  __host__ __device__ static size_t bar_off(int L, int nck) {
+    return ckpt_off(L) + (size_t)(nck > 1 ? nck - 1 : 0) * SP * kBwdThreads * sizeof(float);
+  }
+  __host__ __device__ static size_t total(int L, int nck) { return bar_off(L, nck) + 64; }
+};
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+      "%13, %14, %15, %16};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+      "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15}, [%16];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]),
+        "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]), "=f"(v[14]), "=f"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "f"(v[0]),
+               "f"(v[1]), "f"(v[2]), "f"(v[3])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+                 "=f"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Stores / loads exactly SP consecutive fp32 columns of this thread's TMEM lane
+// (SP a multiple of 4).  Loads are issued back to back and waited for once.
+template <int SP>
+__device__ __forceinline__ void tmem_store(uint32_t taddr, const float (&v)[SP]) {
+#pragma unroll
+  for (int q = 0; q < SP;) {
+    if (SP - q >= 16) {
+      float w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = v[q + i];
+      tmem_st16(taddr + q, w);
+      q += 16;
+    } else if (SP - q >= 8) {
+      tmem_st8(taddr + q, &v[q]);
+      q += 8;
+    } else {
+      tmem_st4(taddr + q, &v[q]);
+      q += 4;
+    }
+  }
+}
+template <int SP>
+__device__ __forceinline__ void tmem_load_nowait(uint32_t taddr, float (&v)[SP]) {
+#pragma unroll
+  for (int q = 0; q < SP;) {
+    if (SP - q >= 16) {
+      float w[16];
+      tmem_ld16(taddr + q, w);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[q + i] = w[i];
+      q += 16;
+    } else if (SP - q >= 8) {
+      tmem_ld8(taddr + q, &v[q]);
+      q += 8;
+    } else {
+      tmem_ld4(taddr + q, &v[q]);
+      q += 4;
+    }
+  }
+}
+
+// Sum of v[i] over the 32 lanes.  Halving butterfly: at each level the lane
+// keeps one half of its values and adds the partner's copy of that half, so 31
+// shuffles reduce 32 values.  Afterwards lane l holds the total of value index
+// (l >> (5 - log2 N)) in v[0] when N <= 32, or indices N/32*l ... in v[0..N/32).
+template <int N, int M>
+struct Halving {
+  static __device__ __forceinline__ void run(float* v, int lane) {
+    if constexpr (M > 0) {
+      if constexpr (N > 1) {
+        constexpr int HN = N / 2;
+        const bool upper = (lane & M) != 0;
+#pragma unroll
+        for (int i = 0; i < HN; ++i) {
+          const float send = upper ? v[i] : v[i + HN];
+          const float keep = upper ? v[i + HN] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, M);
+        }
+        Halving<HN, M / 2>::run(v, lane);
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], M);
+        Halving<1, M / 2>::run(v, lane);
+      }
+    }
+  }
+};
+template <int N>
+__device__ __forceinline__ void warp_halving_reduce(float (&v)[N], int lane) {
+  Halving<N, 16>::run(v, lane);
+}
+
+template <typename T, int SP, bool CLAMP>
+__global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
+  using Cfg = BwdCfg<T, SP>;
+  using Sm = BwdSmem<T, SP>;
+  constexpr int K = Cfg::K, NV = Cfg::NV, NSTAGE = Cfg::NSTAGE;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint32_t s_tmem_base;
+  __shared__ int s_abort;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int L = p.L, D = p.D, S = p.S, nck = p.nck;
+  const int64_t b = blockIdx.x;
+  const int split = blockIdx.y;
+  const int g_begin = split * p.groups_per_cta;
+  const int g_end = min(p.groups, g_begin + p.groups_per_cta);
+  if (g_begin >= g_end) return;  // uniform across the CTA
+
+  T* tiles = reinterpret_cast<T*>(smem + Sm::tiles_off());
+  float* sBf = reinterpret_cast<float*>(smem + Sm::bc_off());  // (L, SP)
+  float* sCf = sBf + (size_t)L * SP;                             // (L, SP)
+  float* slab = reinterpret_cast<float*>(smem + Sm::slab_off(L));  // (4, K, NV)
+  float4* ckpt = reinterpret_cast<float4*>(smem + Sm::ckpt_off(L));  // (nck-1, SP/4, 128)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bar_off(L, nck));
+
+  const T* __restrict__ gx = static_cast<const T*>(p.x);
+  const T* __restrict__ gdt = static_cast<const T*>(p.dt);
+  const T* __restrict__ gdy = static_cast<const T*>(p.dy);
+  const T* __restrict__ gz = static_cast<const T*>(p.z);
+  const bool has_z = p.z != nullptr;
+  const bool has_D = p.Dp != nullptr;
+
+  // ---- set-up: TMEM, barriers, B/C staging -----------------------------------
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    s_abort = 0;
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  {
+    const T* Bm = static_cast<const T*>(p.B) + b * L * S;
+    const T* Cm = static_cast<const T*>(p.C) + b * L * S;
+    for (int i = tid; i < L * SP; i += kBwdThreads) {
+      const int t = i / SP, s = i % SP;
+      sBf[i] = s < S ? io<T>::ld(Bm + (int64_t)t * S + s) : 0.0f;
+      sCf[i] = s < S ? io<T>::ld(Cm + (int64_t)t * S + s) : 0.0f;
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem_base + ((uint32_t)(warp * 32) << 16);
+
+  // ---- tile producer -----------------------------------------------------------
+  // Work items, in order: for each group, nck forward chunks then nck reverse
+  // chunks.  Item i uses stage i % NSTAGE.
+  const int items_per_group = 2 * nck;
+  const int n_items = (g_end - g_begin) * items_per_group;
+  auto issue = [&](int it) {
+    if (it >= n_items) return;
+    const int g = g_begin + it / items_per_group;
+    const int r = it % items_per_group;
+    const bool rev = r >= nck;
+    const int k = rev ? (items_per_group - 1 - r) : r;
+    const int t0 = k * K;
+    const int n = min(K, L - t0);
+    const int c0 = g * kBwdThreads;
+    const int w = min(kBwdThreads, D - c0);
+    const uint32_t row_bytes = (uint32_t)(w * sizeof(T));
+    const int nten = rev ? (has_z ? 4 : 3) : 2;
+    const int stage = it % NSTAGE;
+    T* st = tiles + (size_t)stage * Cfg::NTEN * Cfg::tile_elems;
+    if (warp == 0) {
+      if (lane == 0) mbar_expect_tx(&bars[stage], row_bytes * n * nten);
+      __syncwarp();
+      for (int q = lane; q < n * nten; q += 32) {
+        const int ten = q / n, j = q % n;
+        const T* src = ten == 0 ? gx : ten == 1 ? gdt : ten == 2 ? gdy : gz;
+        src += (b * L + t0 + j) * (int64_t)D + c0;
+        bulk_g2s(st + ((size_t)ten * K + j) * kBwdThreads, src, row_bytes, &bars[stage]);
+      }
+    }
+  };
+  auto wait_item = [&](int it) {
+    const int stage = it % NSTAGE;
+    const uint32_t parity = (it / NSTAGE) & 1;
+    if (!s_abort) {
+      if (!mbar_wait(&bars[stage], parity)) {
+        record_error(p.err, HCLSM_ERR_TIMEOUT);
+        s_abort = 1;
+      }
+    }
+  };
+  for (int i = 0; i < NSTAGE; ++i) issue(i);
+
+  float* dbc_base = p.dBC_ws + ((int64_t)split * p.nseq + b) * L * NV;
+  int it = 0;
+  for (int g = g_begin; g < g_end; ++g) {
+    const int d = g * kBwdThreads + tid;
+    const bool act = d < D;
+    float A[SP], A2[SP], fac[SP];
+#pragma unroll
+    for (int s = 0; s < SP; ++s) {
+      A[s] = 0.0f; A2[s] = 0.0f; fac[s] = 0.0f;
+      if (act && s < S) {
+        const float e = ex2(p.A_log[(int64_t)d * S + s] * kLog2e);
+        const float ec = CLAMP ? fminf(fmaxf(e, 1e-6f), 1.0f) : e;
+        A[s] = -ec;
+        A2[s] = -ec * kLog2e;
+        // dA/dA_log = -exp(A_log), zero where the clamp binds
+        fac[s] = (CLAMP && (e < 1e-6f || e > 1.0f)) ? 0.0f : -e;
+      }
+    }
+    const float Dd = (has_D && act) ? p.Dp[d] : 0.0f;
+
+    // ---- forward sweep: checkpoints ------------------------------------------
+    float h[SP];
+#pragma unroll
+    for (int s = 0; s < SP; ++s) h[s] = 0.0f;
+    for (int k = 0; k < nck; ++k, ++it) {
+      wait_item(it);
+      const T* st = tiles + (size_t)(it % NSTAGE) * Cfg::NTEN * Cfg::tile_elems;
+      const int t0 = k * K, n = min(K, L - t0);
+      if (k > 0) {
+#pragma unroll
+        for (int q = 0; q < SP / 4; ++q)
+          ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid] =
+              make_float4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      }
+      for (int j = 0; j < n; ++j) {
+        float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
+        float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
+        if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
+        const float dtx = dv * xv;
+        const float* Bt = sBf + (size_t)(t0 + j) * SP;
+#pragma unroll
+        for (int s = 0; s < SP; ++s) h[s] = fmaf(ex2(dv * A2[s]), h[s], dtx * Bt[s]);
+      }
+      __syncthreads();
+      if (warp == 0) issue(it + NSTAGE);
+    }
+
+    // ---- reverse sweep --------------------------------------------------------
+    float gcar[SP], gAcc[SP];
+#pragma unroll
+    for (int s = 0; s < SP; ++s) { gcar[s] = 0.0f; gAcc[s] = 0.0f; }
+    float dDacc = 0.0f;
+    for (int k = nck - 1; k >= 0; --k, ++it) {
+      wait_item(it);
+      const T* st = tiles + (size_t)(it % NSTAGE) * Cfg::NTEN * Cfg::tile_elems;
+      const int t0 = k * K, n = min(K, L - t0);
+      // recompute the chunk from its checkpoint, parking h_t and dA_t in TMEM
+      float hs[SP];
+      if (k > 0) {
+#pragma unroll
+        for (int q = 0; q < SP / 4; ++q) {
+          const float4 c4 = ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid];
+          hs[4 * q] = c4.x; hs[4 * q + 1] = c4.y; hs[4 * q + 2] = c4.z; hs[4 * q + 3] = c4.w;
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < SP; ++s) hs[s] = 0.0f;
+      }
+      for (int j = 0; j < n; ++j) {
+        float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
+        float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
+        if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
+        const float dtx = dv * xv;
+        const float* Bt = sBf + (size_t)(t0 + j) * SP;
+        float dA[SP];
+#pragma unroll
+        for (int s = 0; s < SP; ++s) {
+          dA[s] = ex2(dv * A2[s]);
+          hs[s] = fmaf(dA[s], hs[s], dtx * Bt[s]);
+        }
+        const uint32_t col = tmem + (uint32_t)(j * 2 * SP);
+        tmem_store<SP>(col, hs);
+        tmem_store<SP>(col + SP, dA);
+      }
+      tmem_wait_st();
+      // hs == h at the last step of the chunk
+      for (int j = n - 1; j >= 0; --j) {
+        const int t = t0 + j;
+        float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
+        const float draw = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
+        float gy = act ? io<T>::ld(st + ((size_t)2 * K + j) * kBwdThreads + tid) : 0.0f;
+        float dv = draw, mdt = 1.0f;
+        if (CLAMP) {
+          mdt = (draw >= 1e-3f && draw <= 1.0f) ? 1.0f : 0.0f;
+          dv = fminf(fmaxf(draw, 1e-3f), 1.0f);
+        }
+        const float dtx = dv * xv;
+        const float* Bt = sBf + (size_t)t * SP;
+        const float* Ct = sCf + (size_t)t * SP;
+        float dA[SP], hp[SP];
+        const uint32_t col = tmem + (uint32_t)(j * 2 * SP);
+        tmem_load_nowait<SP>(col + SP, dA);
+        if (j > 0) {
+          tmem_load_nowait<SP>(col - 2 * SP, hp);
+        } else if (k > 0) {
+#pragma unroll
+          for (int q = 0; q < SP / 4; ++q) {
+            const float4 c4 = ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid];
+            hp[4 * q] = c4.x; hp[4 * q + 1] = c4.y; hp[4 * q + 2] = c4.z; hp[4 * q + 3] = c4.w;
+          }
+        } else {
+#pragma unroll
+          for (int s = 0; s < SP; ++s) hp[s] = 0.0f;
+        }
+        tmem_wait_ld();
+        float dzv = 0.0f;
+        if (has_z) {
+          const float zv = act ? io<T>::ld(st + ((size_t)3 * K + j) * kBwdThreads + tid) : 0.0f;
+          float ys = 0.0f;
+#pragma unroll
+          for (int s = 0; s < SP; ++s) ys = fmaf(hs[s], Ct[s], ys);
+          ys = fmaf(Dd, xv, ys);
+          const float sg = sigmoid(zv);
+          dzv = gy * ys * sg * (1.0f + zv * (1.0f - sg));
+          gy = gy * zv * sg;
+        }
+        float gB = 0.0f, ddA = 0.0f;
+        float pv[NV];
+#pragma unroll
+        for (int s = 0; s < SP; ++s) {
+          const float gs = fmaf(gy, Ct[s], gcar[s]);
+          gB = fmaf(gs, Bt[s], gB);
+          pv[s] = gs * dtx;
+          pv[SP + s] = gy * hs[s];
+          const float w = dA[s] * gs;
+          const float R = w * hp[s];
+          ddA = fmaf(A[s], R, ddA);
+          gAcc[s] = fmaf(dv, R, gAcc[s]);
+          gcar[s] = w;
+          hs[s] = hp[s];
+        }
+        dDacc = fmaf(gy, xv, dDacc);
+        if (act) {
+          const int64_t gi = (b * L + t) * (int64_t)D + d;
+          io<T>::st(static_cast<T*>(p.dx) + gi, fmaf(dv, gB, Dd * gy));
+          io<T>::st(static_cast<T*>(p.ddt) + gi, fmaf(xv, gB, ddA) * mdt);
+          if (has_z) io<T>::st(static_cast<T*>(p.dz) + gi, dzv);
+        }
+        warp_halving_reduce<NV>(pv, lane);
+        constexpr int kShift = (NV >= 32) ? 0 : (NV == 16 ? 1 : (NV == 8 ? 2 : 3));
+        if (NV >= 32) {
+#pragma unroll
+          for (int i = 0; i < NV / 32; ++i) slab[((size_t)warp * K + j) * NV + lane * (NV / 32) + i] = pv[i];
+        } else if ((lane & ((1 << kShift) - 1)) == 0) {
+          slab[((size_t)warp * K + j) * NV + (lane >> kShift)] = pv[0];
+        }
+      }
+      __syncthreads();
+      // fold the four warps' partial sums into this sequence's dB|dC rows
+      {
+        float* dst = dbc_base + (int64_t)t0 * NV;
+        const bool first = (g == g_begin);
+        for (int e = tid; e < n * NV; e += kBwdThreads) {
+          const int j = e / NV, v = e % NV;
+          float acc = slab[((size_t)0 * K + j) * NV + v] + slab[((size_t)1 * K + j) * NV + v] +
+                      slab[((size_t)2 * K + j) * NV + v] + slab[((size_t)3 * K + j) * NV + v];
+          if (!first) acc += dst[e];
+          dst[e] = acc;
+        }
+      }
+      __syncthreads();
+      if (warp == 0) issue(it + NSTAGE);
+    }
+    if (act) {
+      float* da = p.dAlog_part + (b * D + d) * (int64_t)S;
+#pragma unroll
+      for (int s = 0; s < SP; ++s)
+        if (s < S) da[s] = gAcc[s] * fac[s];
+      if (has_D) p.dD_part[b * D + d] = dDacc;
+    }
+  }
+
+  // ---- tear-down ---------------------------------------------------------------
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// out[c] = sum_r part[r][c] over `rows` rows, deterministic (fixed order).
+// Stage 1 sums row blocks of `rb` rows into part2[blk][c].
+__global__ void colsum_stage1(const float* __restrict__ part, float* __restrict__ part2, int64_t rows,
+                              int64_t cols, int64_t rb) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t blk = blockIdx.y;
+  if (c >= cols) return;
+  const int64_t r0 = blk * rb, r1 = min(rows, r0 + rb);
+  float acc = 0.0f;
+  for (int64_t r = r0; r < r1; ++r) acc += part[r * cols + c];
+  part2[blk * cols + c] = acc;
+}
+__global__ void colsum_stage2(const float* __restrict__ part2, float* __restrict__ out, int64_t nblk,
+                              int64_t cols) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float acc = 0.0f;
+  for (int64_t r = 0; r < nblk; ++r) acc += part2[r * cols + c];
+  out[c] = acc;
+}
+
+// dB/dC: sum the splits' fp32 accumulators and write the output dtype.
+template <typename T>
+__global__ void dbc_finalize(const float* __restrict__ ws, T* __restrict__ dB, T* __restrict__ dC,
+                             int64_t nseq, int L, int S, int SP, int nsplit) {
+  // workspace rows hold 2*SP values per timestep: dB in [0, SP), dC in [SP, 2*SP)
+  const int64_t total = nseq * L * S;
+  const int NV = 2 * SP;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / S;
+    const int s = (int)(i % S);
+    float vb = 0.0f, vc = 0.0f;
+    for (int q = 0; q < nsplit; ++q) {
+      const float* r = ws + ((int64_t)q * nseq * L + row) * NV;
+      vb += r[s];
+      vc += r[SP + s];
+    }
+    io<T>::st(dB + i, vb);
+    io<T>::st(dC + i, vc);
+  }
+}
+
+}  // namespace scan
+}  // namespace hclsm
+
+// ===========================================================================
+// host side
+// ===========================================================================
+namespace hclsm {
+int* device_err_ptr();
+int num_sms();
+bool set_smem_limit(const void* fn, size_t bytes);
+}  // namespace hclsm
+
+namespace hclsm {
+namespace scan {
+
+static int pad_state(int S) {
+  if (S <= 4) return 4;
+  if (S <= 8) return 8;
+  if (S <= 16) return 16;
+  if (S <= 32) return 32;
+  if (S <= 64) return 64;
+  return 0;
+}
+
+template <typename T, int SP, int CPT, bool CLAMP>
+static int launch_fwd_t(FwdParams p, cudaStream_t st) {
+  const int per_cta = kFwdThreads * CPT;
+  const int gx = (p.D + per_cta - 1) / per_cta;
+  const int64_t total = p.nseq;
+  // grid.y is limited to 65535: launch sequence batches
+  for (int64_t s0 = 0; s0 < total; s0 += 65535) {
+    const int64_t ns = std::min<int64_t>(65535, total - s0);
+    FwdParams q = p;
+    const int64_t off = s0 * (int64_t)p.L * p.D, offs = s0 * (int64_t)p.L * p.S;
+    q.x = static_cast<const T*>(p.x) + off;
+    q.dt = static_cast<const T*>(p.dt) + off;
+    q.z = p.z ? static_cast<const T*>(p.z) + off : nullptr;
+    q.y = static_cast<T*>(p.y) + off;
+    q.B = static_cast<const T*>(p.B) + offs;
+    q.C = static_cast<const T*>(p.C) + offs;
+    q.nseq = ns;
+    scan_fwd_kernel<T, SP, CPT, CLAMP><<<dim3(gx, (unsigned)ns), kFwdThreads, 0, st>>>(q);
+  }
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+template <typename T, int SP>
+static int launch_fwd_sp(const FwdParams& p, bool pairs, bool clamp, cudaStream_t st) {
+  if constexpr (SP <= 16) {
+    if (pairs) return clamp ? launch_fwd_t<T, SP, 2, true>(p, st) : launch_fwd_t<T, SP, 2, false>(p, st);
+  }
+  return clamp ? launch_fwd_t<T, SP, 1, true>(p, st) : launch_fwd_t<T, SP, 1, false>(p, st);
+}
+
+template <typename T>
+static int launch_fwd(const FwdParams& p, bool clamp, cudaStream_t st) {
+  const size_t pair_bytes = 2 * sizeof(T);
+  auto al = [&](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) % pair_bytes) == 0; };
+  const bool pairs = (p.D % 2 == 0) && al(p.x) && al(p.dt) && al(p.z) && al(p.y);
+  switch (pad_state(p.S)) {
+    case 4: return launch_fwd_sp<T, 4>(p, pairs, clamp, st);
+    case 8: return launch_fwd_sp<T, 8>(p, pairs, clamp, st);
+    case 16: return launch_fwd_sp<T, 16>(p, pairs, clamp, st);
+    case 32: return launch_fwd_sp<T, 32>(p, pairs, clamp, st);
+    case 64: return launch_fwd_sp<T, 64>(p, pairs, clamp, st);
+  }
+  return HCLSM_ERR_SHAPE;
+}
+
+// ---- backward plan -----------------------------------------------------------
+struct BwdPlan {
+  int SP, K, nck, groups, nsplit, gpc;
+  int64_t nblk, rb;
+  size_t off_dalog, off_dd, off_p2a, off_p2d, off_dbc, total;
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static int bwd_K(int SP) { return std::min(32, 256 / SP); }
+
+static bool plan_bwd(int64_t nseq, int L, int D, int S, BwdPlan* pl) {
+  const int SP = pad_state(S);
+  if (SP == 0 || SP > 16 || nseq <= 0 || L <= 0 || D <= 0) return false;
+  pl->SP = SP;
+  pl->K = bwd_K(SP);
+  pl->nck = (L + pl->K - 1) / pl->K;
+  // checkpoints: (nck-1) * SP * 128 floats must fit 128 KiB
+  if ((int64_t)(pl->nck - 1) * SP * 128 * 4 > 128 * 1024) return false;
+  pl->groups = (D + 127) / 128;
+  const int nsm = num_sms();
+  // choose the channel split that minimises waves x work per CTA; keep the
+  // smallest split within 3 % of the best
+  double best = 1e30;
+  std::vector<std::pair<int, double>> cand;
+  for (int q = 1; q <= pl->groups; ++q) {
+    const int gpc = (pl->groups + q - 1) / q;
+    const int eff = (pl->groups + gpc - 1) / gpc;
+    const double waves = std::ceil((double)nseq * eff / nsm);
+    const double cost = waves * gpc;
+    cand.push_back({eff, cost});
+    best = std::min(best, cost);
+  }
+  pl->nsplit = pl->groups;
+  for (auto& c : cand) {
+    if (c.second <= best * 1.03) { pl->nsplit = c.first; break; }
+  }
+  pl->gpc = (pl->groups + pl->nsplit - 1) / pl->nsplit;
+  pl->nsplit = (pl->groups + pl->gpc - 1) / pl->gpc;
+  pl->nblk = std::min<int64_t>(nseq, 128);
+  pl->rb = (nseq + pl->nblk - 1) / pl->nblk;
+  pl->nblk = (nseq + pl->rb - 1) / pl->rb;
+  size_t off = 0;
+  pl->off_dalog = off; off = align256(off + sizeof(float) * (size_t)nseq * D * S);
+  pl->off_dd = off;    off = align256(off + sizeof(float) * (size_t)nseq * D);
+  pl->off_p2a = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D * S);
+  pl->off_p2d = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D);
+  pl->off_dbc = off;   off = align256(off + sizeof(float) * (size_t)pl->nsplit * nseq * L * 2 * SP);
+  pl->total = off;
+  return true;
+}
+
+template <typename T, int SP, bool CLAMP>
+static int launch_bwd_t(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) {
+  const size_t smem = BwdSmem<T, SP>::total(p.L, p.nck);
+  if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
+  auto fn = scan_bwd_kernel<T, SP, CLAMP>;
+  if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
+  fn<<<dim3((unsigned)p.nseq, pl.nsplit), kBwdThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+template <typename T>
+static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStream_t st) {
+  switch (pl.SP) {
+    case 4: return clamp ? launch_bwd_t<T, 4, true>(p, pl, st) : launch_bwd_t<T, 4, false>(p, pl, st);
+    case 8: return clamp ? launch_bwd_t<T, 8, true>(p, pl, st) : launch_bwd_t<T, 8, false>(p, pl, st);
+    case 16: return clamp ? launch_bwd_t<T, 16, true>(p, pl, st) : launch_bwd_t<T, 16, false>(p, pl, st);
+  }
+  return HCLSM_ERR_SHAPE;
+}
+
+}  // namespace scan
+}  // namespace hclsm
+
+using namespace hclsm;
+using namespace hclsm::scan;
+
+static bool aligned16(const void* q) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % 16 == 0; }
+
+extern "C" int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_log, const void* B,
+                                  const void* C, const float* D, const void* z, void* y, int64_t nseq,
+                                  int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype, int32_t clamp,
+                                  void* stream) {
+  if (!x || !dt || !A_log || !B || !C || !y) return HCLSM_ERR_NULL;
+  if (nseq < 0 || L < 0 || d_inner < 0 || d_state <= 0 || d_state > 64) return HCLSM_ERR_SHAPE;
+  if (nseq == 0 || L == 0 || d_inner == 0) return HCLSM_OK;
+  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == HCLSM_F32) return launch_fwd<float>(p, clamp != 0, st);
+  if (dtype == HCLSM_BF16) return launch_fwd<__nv_bfloat16>(p, clamp != 0, st);
+  return HCLSM_ERR_DTYPE;
+}
+
+extern "C" size_t hclsm_ssm_scan_bwd_workspace_size(int64_t nseq, int32_t L, int32_t d_inner,
+                                                    int32_t d_state) {
+  BwdPlan pl;
+  if (!plan_bwd(nseq, L, d_inner, d_state, &pl)) return 0;
+  return pl.total;
+}
+
+extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const void* B,
+                                  const void* C, const float* D, const void* z, const void* dy, void* dx,
+                                  void* ddt, float* dA_log, void* dB, void* dC, float* dD, void* dz,
+                                  int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype,
+                                  int32_t clamp, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !dt || !A_log || !B || !C || !dy || !dx || !ddt || !dA_log || !dB || !dC) return HCLSM_ERR_NULL;
+  if (D && !dD) return HCLSM_ERR_NULL;
+  if (z && !dz) return HCLSM_ERR_NULL;
+  if (nseq < 0 || L < 0 || d_inner <= 0 || d_state <= 0) return HCLSM_ERR_SHAPE;
+  if (dtype != HCLSM_F32 && dtype != HCLSM_BF16) return HCLSM_ERR_DTYPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (nseq == 0 || L == 0) {
+    cudaMemsetAsync(dA_log, 0, sizeof(float) * (size_t)d_inner * d_state, st);
+    if (D) cudaMemsetAsync(dD, 0, sizeof(float) * (size_t)d_inner, st);
+    return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  }
+  BwdPlan pl;
+  if (!plan_bwd(nseq, L, d_inner, d_state, &pl)) return HCLSM_ERR_UNSUPPORTED;
+  if (nseq > 2147483647LL) return HCLSM_ERR_SHAPE;
+  const size_t esz = dtype == HCLSM_F32 ? 4 : 2;
+  // rows of x/dt/dy/z are fetched by 16-byte bulk copies
+  if ((d_inner * esz) % 16 != 0) return HCLSM_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(dt) || !aligned16(dy) || !aligned16(z)) return HCLSM_ERR_ALIGN;
+  if (!workspace || workspace_bytes < pl.total) return HCLSM_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return HCLSM_ERR_ALIGN;
+  char* ws = static_cast<char*>(workspace);
+  BwdParams p;
+  p.x = x; p.dt = dt; p.A_log = A_log; p.B = B; p.C = C; p.Dp = D; p.z = z; p.dy = dy;
+  p.dx = dx; p.ddt = ddt; p.dz = dz;
+  p.dAlog_part = reinterpret_cast<float*>(ws + pl.off_dalog);
+  p.dD_part = reinterpret_cast<float*>(ws + pl.off_dd);
+  p.dBC_ws = reinterpret_cast<float*>(ws + pl.off_dbc);
+  p.nseq = nseq; p.L = L; p.D = d_inner; p.S = d_state;
+  p.nck = pl.nck; p.groups = pl.groups; p.groups_per_cta = pl.gpc; p.nsplit = pl.nsplit;
+  p.err = device_err_ptr();
+  int rc = dtype == HCLSM_F32 ? launch_bwd<float>(p, pl, clamp != 0, st)
+                              : launch_bwd<__nv_bfloat16>(p, pl, clamp != 0, st);
+  if (rc != HCLSM_OK) return rc;
+  // dA_log and dD: deterministic column sums over sequences
+  {
+    const int64_t cols = (int64_t)d_inner * d_state;
+    float* p2 = reinterpret_cast<float*>(ws + pl.off_p2a);
+    colsum_stage1<<<dim3((unsigned)((cols + 255) / 256), (unsigned)pl.nblk), 256, 0, st>>>(
+        p.dAlog_part, p2, nseq, cols, pl.rb);
+    colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(p2, dA_log, pl.nblk, cols);
+  }
+  if (D) {
+    const int64_t cols = d_inner;
+    float* p2 = reinterpret_cast<float*>(ws + pl.off_p2d);
+    colsum_stage1<<<dim3((unsigned)((cols + 255) / 256), (unsigned)pl.nblk), 256, 0, st>>>(
+        p.dD_part, p2, nseq, cols, pl.rb);
+    colsum_stage2<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(p2, dD, pl.nblk, cols);
+  }
+  {
+    const int64_t total = nseq * (int64_t)L * d_state;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    if (dtype == HCLSM_F32)
+      dbc_finalize<float><<<blocks, 256, 0, st>>>(p.dBC_ws, static_cast<float*>(dB), static_cast<float*>(dC),
+                                                  nseq, L, d_state, pl.SP, pl.nsplit);
+    else
+      dbc_finalize<__nv_bfloat16><<<blocks, 256, 0, st>>>(p.dBC_ws, static_cast<__nv_bfloat16*>(dB),
+                                                          static_cast<__nv_bfloat16*>(dC), nseq, L, d_state,
+                                                          pl.SP, pl.nsplit);
+  }
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}

@@ -1,0 +1,62 @@
+"""Seeded synthetic workloads with the shapes and value distributions of the
+five benchmark configurations (no datasets are involved).
+
+All generators draw fp32 values from a ``torch.Generator`` seeded per call and
+cast afterwards, so a CPU oracle fed the cast tensors sees identical bits.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+
+@dataclass(frozen=True)
+class ScanConfig:
+    name: str
+    videos: int
+    slots: int
+    L: int
+    d_inner: int
+    d_state: int
+    dtype: torch.dtype
+    backward: bool
+    clamp: bool
+
+    @property
+    def nseq(self) -> int:
+        return self.videos * self.slots
+
+
+# Config 0 runs the CPU dispatch in the reference (sequential_ssm_scan, clamped);
+# configs 1 and 4 follow the reference's CUDA semantics (unclamped).
+SCAN_CONFIGS = {
+    0: ScanConfig("tiny scan fwd fp32", 2, 16, 16, 512, 16, torch.float32, False, True),
+    1: ScanConfig("small scan fwd+bwd bf16", 8, 32, 64, 768, 16, torch.bfloat16, True, False),
+    4: ScanConfig("base scan fwd+bwd bf16", 64, 128, 256, 2048, 16, torch.bfloat16, True, False),
+}
+
+
+def scan_inputs(nseq, L, d_inner, d_state, dtype=torch.float32, seed=0, device="cpu", gated=False,
+                grad=True):
+    """x, B, C ~ N(0,1); dt = softplus(N(0,1) - 2); A_log ~ U(0, ln 16) so that
+    A = -exp(A_log) in [-16, -1]; D, z, dy ~ N(0,1).  A_log and D stay fp32."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device=device, dtype=torch.float32)
+
+    out = {}
+    out["x"] = randn(nseq, L, d_inner).to(dtype)
+    out["dt"] = F.softplus(randn(nseq, L, d_inner) - 2.0).to(dtype)
+    out["A_log"] = torch.rand(d_inner, d_state, generator=g, device=device) * math.log(16.0)
+    out["B"] = randn(nseq, L, d_state).to(dtype)
+    out["C"] = randn(nseq, L, d_state).to(dtype)
+    if gated:
+        out["D"] = randn(d_inner)
+        out["z"] = randn(nseq, L, d_inner).to(dtype)
+    if grad:
+        out["dy"] = randn(nseq, L, d_inner).to(dtype)
+    return out

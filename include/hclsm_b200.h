@@ -1,0 +1,90 @@
+/*
+ * hclsm_b200 — C ABI of the B200 (sm_100a) kernels behind HCLSM's data-parallel
+ * hot path: the Level-0 selective SSM scan (forward and backward), the fused
+ * slot-attention iteration and the sparse event attention.
+ *
+ * Conventions for every entry point:
+ *   - pointers are device pointers unless stated; tensors are dense row-major;
+ *   - `stream` is a cudaStream_t passed as void*; every call is stream-ordered,
+ *     never synchronises and allocates nothing (callers pass workspaces);
+ *   - the return value is an hclsm_status; nothing traps.  A kernel whose
+ *     bounded wait ran out records HCLSM_ERR_TIMEOUT in a per-device error
+ *     word that hclsm_device_error() reads (that call synchronises).
+ *
+ * Reference interfaces (paths inside the RightNow-AI/hclsm project):
+ *   hclsm/kernels/ssm_scan_kernel.py, slot_attention_kernel.py,
+ *   sparse_event_attn.py; hclsm/objects/dynamic_slots.py;
+ *   hclsm/dynamics/level1_event.py, hierarchy_manager.py.
+ */
+#ifndef HCLSM_B200_H_
+#define HCLSM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  HCLSM_OK = 0,
+  HCLSM_ERR_SHAPE = 1,       /* a size is out of the supported range */
+  HCLSM_ERR_DTYPE = 2,       /* unknown dtype code */
+  HCLSM_ERR_ALIGN = 3,       /* a pointer is not aligned as required */
+  HCLSM_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+  HCLSM_ERR_LAUNCH = 5,      /* a CUDA launch failed (see cudaGetLastError) */
+  HCLSM_ERR_TIMEOUT = 6,     /* a device-side bounded wait ran out */
+  HCLSM_ERR_UNSUPPORTED = 7, /* valid input this build does not handle */
+  HCLSM_ERR_NULL = 8         /* a required pointer is NULL */
+} hclsm_status;
+
+typedef enum { HCLSM_F32 = 0, HCLSM_BF16 = 1 } hclsm_dtype;
+
+/* Library version and the per-device error word.  hclsm_device_error
+ * synchronises the device, returns the first recorded error code (0 if none)
+ * and clears it. */
+int hclsm_version(void);
+int hclsm_device_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Selective SSM scan, forward.
+ * Replaces hclsm/kernels/ssm_scan_kernel.py:394 ssm_scan_fn (the dispatcher),
+ * with the arithmetic of sequential_ssm_scan :42-86 (clamp=1) or of
+ * parallel_ssm_scan_pytorch :168-218 / _ssm_scan_fwd_kernel :227-290 (clamp=0).
+ *   x, dt, y, z : (nseq, L, d_inner)   dtype
+ *   B, C        : (nseq, L, d_state)   dtype
+ *   A_log       : (d_inner, d_state)   f32
+ *   D           : (d_inner,)           f32, optional (NULL)
+ *   z           : optional (NULL); when given y = (scan + D*x) * silu(z)
+ * d_state <= 64.  State and arithmetic are fp32 for both dtypes.
+ * ------------------------------------------------------------------------- */
+int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_log, const void* B,
+                       const void* C, const float* D, const void* z, void* y, int64_t nseq,
+                       int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype, int32_t clamp,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Selective SSM scan, backward.
+ * Replaces hclsm/kernels/ssm_scan_kernel.py:321-377 _TritonSSMScan.backward
+ * (clamp=0) and the autograd of sequential_ssm_scan (clamp=1).
+ * Inputs as for the forward plus dy (nseq, L, d_inner).  Outputs:
+ *   dx, ddt, dz : (nseq, L, d_inner) dtype  (dz only when z != NULL)
+ *   dB, dC      : (nseq, L, d_state) dtype
+ *   dA_log      : (d_inner, d_state) f32
+ *   dD          : (d_inner,)         f32  (only when D != NULL)
+ * `workspace` must hold hclsm_ssm_scan_bwd_workspace_size(...) bytes.
+ * Supported: d_state in {4, 8, 16} with L <= 256*256/(d_state*d_state)
+ * (L <= 256 at d_state 16).
+ * ------------------------------------------------------------------------- */
+size_t hclsm_ssm_scan_bwd_workspace_size(int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state);
+int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const void* B, const void* C,
+                       const float* D, const void* z, const void* dy, void* dx, void* ddt,
+                       float* dA_log, void* dB, void* dC, float* dD, void* dz, int64_t nseq,
+                       int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype, int32_t clamp,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HCLSM_B200_H_ */

@@ -1,0 +1,195 @@
+"""Generate golden vectors from the reference implementation itself.
+
+Run in a container that has the reference source tree (pure Python + torch):
+
+    python tests/golden/make_golden.py --reference <path to RightNow-AI/hclsm>
+
+Writes ``tests/golden/*.npz``.  Each case stores its inputs and the reference's
+outputs, computed on CPU in fp32 by the reference functions named in the key.
+The oracle (``oracle/``) is pinned against these files by
+``tests/test_oracle_golden.py``; nothing at test or bench time needs the
+reference tree.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _np(t):
+    return t.detach().cpu().float().numpy().copy()
+
+
+def scan_cases():
+    from hclsm.kernels import ssm_scan_kernel as sk
+
+    out = {}
+    # (a) the reference test fixtures, tests/test_kernels.py:120-128 distributions
+    shapes = [(2, 16, 32, 8), (1, 8, 64, 16), (4, 32, 16, 4)]
+    for ci, (Bn, T, d, s) in enumerate(shapes):
+        g = torch.Generator().manual_seed(100 + ci)
+        x = torch.randn(Bn, T, d, generator=g)
+        dt = torch.rand(Bn, T, d, generator=g).abs() + 0.01
+        A_log = torch.randn(d, s, generator=g)
+        Bp = torch.randn(Bn, T, s, generator=g)
+        C = torch.randn(Bn, T, s, generator=g)
+        dy = torch.randn(Bn, T, d, generator=g)
+        out.update(_scan_case(sk, f"test{ci}", x, dt, A_log, Bp, C, dy))
+    # (b) BASELINE value distributions (configs 0/1/4) at a small size
+    g = torch.Generator().manual_seed(7)
+    Bn, T, d, s = 4, 24, 64, 16
+    x = torch.randn(Bn, T, d, generator=g)
+    dt = F.softplus(torch.randn(Bn, T, d, generator=g) - 2.0)
+    A_log = torch.empty(d, s).uniform_(0.0, float(np.log(16.0)), generator=g)
+    Bp = torch.randn(Bn, T, s, generator=g)
+    C = torch.randn(Bn, T, s, generator=g)
+    dy = torch.randn(Bn, T, d, generator=g)
+    Dv = torch.randn(d, generator=g)
+    z = torch.randn(Bn, T, d, generator=g)
+    out.update(_scan_case(sk, "base", x, dt, A_log, Bp, C, dy, Dv=Dv, z=z))
+    return out
+
+
+def _scan_case(sk, name, x, dt, A_log, Bp, C, dy, Dv=None, z=None):
+    o = {f"{name}/x": _np(x), f"{name}/dt": _np(dt), f"{name}/A_log": _np(A_log), f"{name}/B": _np(Bp),
+         f"{name}/C": _np(C), f"{name}/dy": _np(dy)}
+    # forward: sequential (CPU dispatch; clamped) and parallel (GPU semantics)
+    o[f"{name}/y_sequential"] = _np(sk.sequential_ssm_scan(x, dt, A_log, Bp, C))
+    o[f"{name}/y_parallel"] = _np(sk.parallel_ssm_scan_pytorch(x, dt, A_log, Bp, C))
+    # backward: autograd through both
+    for tag, fn in (("sequential", sk.sequential_ssm_scan), ("parallel", sk.parallel_ssm_scan_pytorch)):
+        leaves = [t.clone().requires_grad_(True) for t in (x, dt, A_log, Bp, C)]
+        y = fn(*leaves)
+        y.backward(dy)
+        for k, t in zip(("dx", "ddt", "dA_log", "dB", "dC"), leaves):
+            o[f"{name}/{k}_{tag}"] = _np(t.grad)
+    # backward: _TritonSSMScan.backward called directly (its body is PyTorch)
+    if hasattr(sk, "_TritonSSMScan"):
+        class Ctx:
+            pass
+        ctx = Ctx()
+        ctx.saved_tensors = (x.float(), dt.float(), A_log, Bp.float(), C.float(), None)
+        grads = sk._TritonSSMScan.backward(ctx, dy)
+        for k, t in zip(("dx", "ddt", "dA_log", "dB", "dC"), grads):
+            o[f"{name}/{k}_tritonbwd"] = _np(t)
+    if Dv is not None:
+        # composed extension: y_out = (scan + D*x) * silu(z), gate form of
+        # hclsm/dynamics/level0_ssm.py:73,104 — built from the reference scan
+        o[f"{name}/D"] = _np(Dv)
+        o[f"{name}/z"] = _np(z)
+        leaves = [t.clone().requires_grad_(True) for t in (x, dt, A_log, Bp, C, Dv, z)]
+        xs, dts, As, Bs, Cs, Ds, zs = leaves
+        y = (sk.parallel_ssm_scan_pytorch(xs, dts, As, Bs, Cs) + Ds * xs) * F.silu(zs)
+        y.backward(dy)
+        o[f"{name}/y_gated"] = _np(y)
+        for k, t in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), leaves):
+            o[f"{name}/{k}_gated"] = _np(t.grad)
+    return o
+
+
+def slot_cases():
+    from hclsm.kernels.slot_attention_kernel import naive_slot_attention
+    from hclsm.config import ObjectConfig
+    from hclsm.objects.dynamic_slots import DynamicSlotAttention
+
+    out = {}
+    for ci, (Bn, N, M, D) in enumerate([(2, 16, 64, 128), (1, 8, 32, 64), (2, 32, 49, 64)]):
+        g = torch.Generator().manual_seed(200 + ci)
+        Q = torch.randn(Bn, N, D, generator=g)
+        K = torch.randn(Bn, M, D, generator=g)
+        V = torch.randn(Bn, M, D, generator=g)
+        o, a = naive_slot_attention(Q, K, V)
+        out.update({f"core{ci}/Q": _np(Q), f"core{ci}/K": _np(K), f"core{ci}/V": _np(V),
+                    f"core{ci}/out": _np(o), f"core{ci}/attn": _np(a)})
+    # DynamicSlotAttention._iteration_step x 3 (hclsm/objects/dynamic_slots.py:98-131)
+    g = torch.Generator().manual_seed(300)
+    F_, N, M, D = 3, 8, 49, 64
+    cfg = ObjectConfig(d_slot=D, n_max_slots=N, n_iterations=3)
+    mod = DynamicSlotAttention(cfg, d_input=D)
+    with torch.no_grad():
+        for name, p in mod.named_parameters():
+            if "norm" in name:
+                continue  # LayerNorm affine stays at gamma=1, beta=0
+            p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    slots = torch.randn(F_, N, D, generator=g)
+    k = torch.randn(F_, M, D, generator=g)
+    v = torch.randn(F_, M, D, generator=g)
+    out["iter/slots0"] = _np(slots)
+    out["iter/k"] = _np(k)
+    out["iter/v"] = _np(v)
+    for name, p in mod.named_parameters():
+        out[f"iter/w/{name}"] = _np(p)
+    s = slots
+    with torch.no_grad():
+        for i in range(3):
+            s = mod._iteration_step(s, k, v)
+            out[f"iter/slots{i + 1}"] = _np(s)
+    return out
+
+
+def event_cases():
+    from hclsm.config import Level1Config
+    from hclsm.dynamics.level1_event import Level1EventDynamics
+    from hclsm.dynamics.hierarchy_manager import HierarchyManager
+    from hclsm.kernels.sparse_event_attn import naive_sparse_event_attention, sparse_event_attention
+
+    out = {}
+    g = torch.Generator().manual_seed(400)
+    Bn, T, N, D = 3, 10, 6, 64
+    cfg = Level1Config(d_model=64, n_layers=2, n_heads=4)
+    l1 = Level1EventDynamics(cfg, d_slot=D)
+    with torch.no_grad():
+        for name, p in l1.named_parameters():
+            if "norm" in name:
+                continue
+            p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    l1.eval()
+    states = torch.randn(Bn, T, N, D, generator=g)
+    mask = (torch.rand(Bn, T, generator=g) < 0.3).float()
+    mask[2] = 0.0
+    mask[2, 0] = 1.0  # at least one event per video, as event_detector.py:167-170 forces
+    # Level1EventDynamics.forward takes (B, K, N, D) (level1_event.py:101) while
+    # sparse_event_attn_fn hands attn_fn a (B*K, N, D) tensor
+    # (sparse_event_attn.py:73-74); each event frame is processed on its own, so
+    # the adapter runs it as K=1.
+    def attn_fn(f):
+        return l1(f[:, None])[:, 0]
+
+    with torch.no_grad():
+        y_naive = naive_sparse_event_attention(states, mask, attn_fn)
+        y_vec = sparse_event_attention(states, mask, attn_fn)
+        hm = HierarchyManager(D, 32)
+        ev, pad, kmax = hm.gather_events(states, mask)
+        alive = torch.ones(Bn, N)
+        alive[1, 4:] = 0.0
+        upd = l1(ev, pad, alive)
+        y_model = hm.scatter_events(states, upd, mask)
+    out.update({"ev/states": _np(states), "ev/mask": _np(mask), "ev/y_naive": _np(y_naive),
+                "ev/y_vectorized": _np(y_vec), "ev/alive": _np(alive), "ev/y_model": _np(y_model),
+                "ev/n_heads": np.array(cfg.n_heads), "ev/n_layers": np.array(cfg.n_layers)})
+    for name, p in l1.named_parameters():
+        out[f"ev/w/{name}"] = _np(p)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    torch.set_num_threads(1)
+    np.savez_compressed(os.path.join(HERE, "scan_golden.npz"), **scan_cases())
+    np.savez_compressed(os.path.join(HERE, "slot_golden.npz"), **slot_cases())
+    np.savez_compressed(os.path.join(HERE, "event_golden.npz"), **event_cases())
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+
+
+if __name__ == "__main__":
+    main()
