@@ -1,0 +1,319 @@
+"""Benchmark of the HCLSM hot path on B200: selective-scan forward+backward at
+BASELINE config 4 (per GPU: 8192 sequences = 64 videos x 128 slots, L=256,
+d_inner=2048, d_state=16, bf16 I/O, fp32 state).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N>1 runs under torchrun, one process per GPU; every rank scans its own 8192
+sequences (sequences are independent: no collective on the data path) and the
+whole-job throughput is total sequences / max-over-ranks device time.
+
+Output: one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L, DI, DS = 256, 2048, 16
+SEQS_PER_GPU = 8192
+# Algorithmic bytes per sequence (bf16 I/O).  Forward reads x, dt, B, C and
+# writes y; backward reads x, dt, dy, B, C and writes dx, ddt, dB, dC.  A_log
+# (read) and dA_log (written), fp32, are counted once per call.
+FWD_BYTES_PER_SEQ = 3 * L * DI * 2 + 2 * L * DS * 2
+BWD_BYTES_PER_SEQ = 5 * L * DI * 2 + 4 * L * DS * 2
+ALOG_BYTES = DI * DS * 4
+# DRAM bytes per sequence of the backward kernel measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum, 148-sequence config-4 slice;
+# see profiles/scan_config4_slice_ncu.md).
+BWD_TRAFFIC_PER_SEQ = 5.30e6
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU, help="sequences per GPU")
+    ap.add_argument("--e2e-seqs", type=int, default=1024, help="sequences per rank in the end-to-end leg")
+    ap.add_argument("--ref-seqs", type=int, default=16, help="sequences per CPU-baseline step")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def cpu_reference(nseq, steps, warmup):
+    """Time the CPU restatement of the reference scan (fwd + bwd) on a bounded
+    sample of the config-4 workload, using every host core."""
+    import torch
+
+    from hclsm_b200.workloads import scan_inputs
+    from oracle import scan as oscan
+
+    threads = oscan.default_threads()
+    d = scan_inputs(nseq, L, DI, DS, dtype=torch.bfloat16, seed=1234)
+    o = {k: v.float().numpy() for k, v in d.items()}
+
+    def step():
+        oscan.scan_fwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], threads=threads)
+        oscan.scan_bwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o["dy"], threads=threads)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    return nseq * steps / dt, threads, dt / steps
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-i", str(index), "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(self.NAMES, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import hclsm_b200
+    from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, scan_bwd_raw, scan_fwd_raw
+    from hclsm_b200.workloads import scan_inputs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    nseq = args.seqs
+    d = scan_inputs(nseq, L, DI, DS, dtype=torch.bfloat16, seed=1000 + rank, device=dev)
+    ws = torch.empty(bwd_workspace_bytes(nseq, L, DI, DS), dtype=torch.uint8, device=dev)
+    y = torch.empty_like(d["x"])
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y)
+        return scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws)
+
+    for _ in range(args.warmup):
+        g = step()
+    del g
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local_rank) if rank == 0 else None
+    if clocks:
+        time.sleep(0.3)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ev[0].record(stream)
+    for i in range(args.steps):
+        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y)
+        ev[2 * i + 1].record(stream)
+        g = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws)
+        ev[2 * i + 2].record(stream)
+        del g
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    total_ms = ev[0].elapsed_time(ev[2 * args.steps])
+    fwd_ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps
+    bwd_ms = sum(ev[2 * i + 1].elapsed_time(ev[2 * i + 2]) for i in range(args.steps)) / args.steps
+    t = torch.tensor([total_ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, fwd_ms, bwd_ms = t.tolist()
+    err = hclsm_b200.device_error()
+    if err:
+        raise RuntimeError(f"device error {err}")
+    del d, ws, y
+    torch.cuda.empty_cache()
+    e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)
+    return dict(ms_per_step=total_ms / args.steps, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk, e2e=e2e)
+
+
+def run_e2e(args, rank, world, dev):
+    """Inputs in pinned host memory; per step: H2D copy, forward + backward via
+    ``ssm_scan_fn`` and autograd, D2H copy of y and every gradient.  Chunks of
+    sequences are pipelined over a copy stream and the compute stream."""
+    import torch
+    import torch.distributed as dist
+
+    from hclsm_b200.kernels import ssm_scan_fn
+    from hclsm_b200.workloads import scan_inputs
+
+    n = args.e2e_seqs
+    chunk = min(256, n)
+    host = {k: v.pin_memory() for k, v in scan_inputs(n, L, DI, DS, dtype=torch.bfloat16, seed=77 + rank).items()}
+    outs = {k: torch.empty_like(host["x"]).pin_memory() for k in ("y", "dx", "ddt")}
+    outs.update({k: torch.empty_like(host["B"]).pin_memory() for k in ("dB", "dC")})
+    dA_host = torch.empty(DI, DS, dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = sum(v.numel() * v.element_size() for v in outs.values()) + dA_host.numel() * 4
+    cs = torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+
+    def step():
+        A = host["A_log"].to(dev, non_blocking=True).requires_grad_(True)
+        for s0 in range(0, n, chunk):
+            s1 = min(n, s0 + chunk)
+            with torch.cuda.stream(cs):
+                dv = {k: host[k][s0:s1].to(dev, non_blocking=True) for k in ("x", "dt", "B", "C", "dy")}
+                ready = torch.cuda.Event()
+                ready.record(cs)
+            comp.wait_event(ready)
+            for v in dv.values():
+                v.record_stream(comp)
+            leaves = [dv[k].requires_grad_(True) for k in ("x", "dt", "B", "C")]
+            y = ssm_scan_fn(leaves[0], leaves[1], A, leaves[2], leaves[3])
+            torch.autograd.backward(y, dv["dy"])
+            done = torch.cuda.Event()
+            done.record(comp)
+            with torch.cuda.stream(cs):
+                cs.wait_event(done)
+                for k, t in (("y", y), ("dx", leaves[0].grad), ("ddt", leaves[1].grad),
+                             ("dB", leaves[2].grad), ("dC", leaves[3].grad)):
+                    outs[k][s0:s1].copy_(t.detach(), non_blocking=True)
+                    t.record_stream(cs)
+        comp.wait_stream(cs)
+        dA_host.copy_(A.grad, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for _ in range(args.steps):
+        step()
+    e1.record(comp)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    return {"value": n * world / (ms * 1e-3), "unit": "sequences/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "sequences_per_rank": n}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    args.warmup = max(args.warmup, 3)
+    metric = "ssm_scan_fwd_bwd_throughput"
+    config = {"workload": "BASELINE config 4: selective scan fwd+bwd, 64 videos x 128 slots = 8192 sequences "
+                          "per GPU, L=256, d_inner=2048, d_state=16, bf16 I/O / fp32 state",
+              "sequences_per_gpu": args.seqs, "global_sequences": args.seqs * world, "L": L,
+              "d_inner": DI, "d_state": DS, "parallelism": f"sequence-sharded x{world}",
+              "l2": "inputs (8.6 GB per tensor) are larger than L2; no flush needed"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        val, cores, step_s = cpu_reference(args.ref_seqs, args.steps, 1)
+        line = {"metric": metric, "value": val, "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "impl": "reference",
+                "cpu_baseline": {"value": val, "unit": "sequences/s", "cores": cores, "kind": "port",
+                                 "sample": f"{args.ref_seqs} config-4 sequences fwd+bwd per step (C restatement "
+                                           f"of the reference scan on bf16-rounded inputs, fp32 arithmetic)"},
+                "e2e": {"value": val, "unit": "sequences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    r = run_b200(args, rank, world, local_rank)
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        v, cores, _ = cpu_reference(args.ref_seqs, 1, 1)
+        cpu = {"value": v, "unit": "sequences/s", "cores": cores, "kind": "port",
+               "sample": f"{args.ref_seqs} config-4 sequences fwd+bwd (C restatement of the reference scan)"}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        ms = r["ms_per_step"]
+        fwd_bytes = args.seqs * FWD_BYTES_PER_SEQ + ALOG_BYTES
+        bwd_bytes = args.seqs * BWD_BYTES_PER_SEQ + 2 * ALOG_BYTES
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        hbm_peak = peaks.get("hbm_gbs", 6650.0)
+        bw_bwd = bwd_bytes / (r["bwd_ms"] * 1e-3) / 1e9
+        bw_fwd = fwd_bytes / (r["fwd_ms"] * 1e-3) / 1e9
+        line = {"metric": metric, "value": args.seqs * world / (ms * 1e-3), "unit": "sequences/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config,
+                "hbm_gbs_algorithmic": (fwd_bytes + bwd_bytes) * world / (ms * 1e-3) / 1e9,
+                "roofline": {"bound": "hbm", "kernel": "scan_bwd_kernel (hclsm_ssm_scan_bwd)",
+                             "achieved": bw_bwd, "peak": hbm_peak, "unit": "GB/s", "frac": bw_bwd / hbm_peak,
+                             "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                             "traffic": BWD_TRAFFIC_PER_SEQ * args.seqs, "algorithmic_bytes": bwd_bytes,
+                             "ms": r["bwd_ms"]},
+                "roofline_fwd": {"kernel": "scan_fwd (hclsm_ssm_scan_fwd)", "achieved": bw_fwd,
+                                 "frac": bw_fwd / hbm_peak, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes},
+                "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
+                "gpu_launches": 5 * args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
