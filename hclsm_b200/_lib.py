@@ -37,6 +37,8 @@ SIGNATURES = {
     "hclsm_ssm_scan_fwd": (ctypes.c_int, [_vp] * 8 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "hclsm_ssm_scan_bwd_workspace_size": (_sz, [_i64, _i32, _i32, _i32]),
     "hclsm_ssm_scan_bwd": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "hclsm_ssm_scan_bwd_noalloc_max_scratch": (_sz, []),
+    "hclsm_ssm_scan_bwd_noalloc": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
 }
 
 _lib = None

@@ -83,6 +83,25 @@ int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const 
                        int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype, int32_t clamp,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Selective SSM scan, backward, without a caller workspace.
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory when they run the backward (host callbacks, allocator
+ * hooks, runtimes with a fixed memory plan).  Same arguments and outputs as
+ * hclsm_ssm_scan_bwd minus the workspace; the scratch lives in a fixed device
+ * array of hclsm_ssm_scan_bwd_noalloc_max_scratch() bytes (48 MiB) that every
+ * GPU loading the library holds until exit.  Returns HCLSM_ERR_WORKSPACE when
+ * the problem needs more scratch than that.  Calls on one device share the
+ * array: calls that overlap on the GPU race.  The first call on a device
+ * resolves the array's address; make it before any stream capture.
+ * ------------------------------------------------------------------------- */
+size_t hclsm_ssm_scan_bwd_noalloc_max_scratch(void);
+int hclsm_ssm_scan_bwd_noalloc(const void* x, const void* dt, const float* A_log, const void* B,
+                               const void* C, const float* D, const void* z, const void* dy, void* dx,
+                               void* ddt, float* dA_log, void* dB, void* dC, float* dD, void* dz,
+                               int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype,
+                               int32_t clamp, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
