@@ -322,6 +322,8 @@ struct BwdParams {
   int groups;          // number of 128-channel groups
   int groups_per_cta;  // contiguous groups handled by one CTA
   int nsplit;
+  float* ckpt_ws;   // packed bf16 kernel: per-SM checkpoint slots
+  int ckpt_slots;
   int* err;
 };
 
@@ -746,6 +748,433 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// backward, bf16 I/O and d_state <= 16: packed variant, 8 warps
+// ---------------------------------------------------------------------------
+// Same algorithm as scan_bwd_kernel, reorganised for issue efficiency:
+//  * a CTA has 256 threads (two warps per SM sub-partition), one channel and
+//    all 16 states per thread, so per-timestep scalar work (loads, clamps,
+//    stores, reductions) is shared by 16 states;
+//  * warps w and w+4 share a TMEM lane quarter and split its 512 columns: 10
+//    steps of history per thread, h_t as fp32 and dA_t as f16x2 (24 columns
+//    per step);
+//  * the sqrt(L) checkpoints of h (every 10 steps) live in a per-SM slot of
+//    the workspace (blocks run one per SM, slot = %smid), which stays resident
+//    in L2; the next chunk's checkpoint is fetched while a chunk is processed;
+//  * per-state arithmetic runs on state pairs (FFMA2 / FMUL2); exp(dt*A) is one
+//    f16x2 SFU op per pair;
+//  * in the dB/dC warp reduction, lane l keeps state s in register slot
+//    s ^ (l & 12), so the levels that exchange across lane bits 3 and 2 keep
+//    slots [0, n/2) without selects.
+constexpr int kW16Threads = 256;
+constexpr int kW16Ch = 256;   // channels per group
+constexpr int kW16K = 10;     // history steps per chunk
+constexpr int kW16Cols = 24;  // TMEM columns per step: 16 x h (f32) + 8 x dA (f16x2)
+constexpr int kW16MaxSlots = 1024;
+
+struct W16Smem {
+  __host__ __device__ static size_t tile_elems() { return (size_t)kW16K * kW16Ch; }
+  __host__ __device__ static size_t tiles_bytes() { return 2 * 4 * tile_elems() * 2; }
+  __host__ __device__ static size_t bc_off() { return tiles_bytes(); }
+  __host__ __device__ static size_t slab_off(int L) { return bc_off() + (size_t)L * 16 * 2 * 4; }
+  __host__ __device__ static size_t dbc_off(int L) { return slab_off(L) + 8 * (size_t)kW16K * 32 * 4; }
+  __host__ __device__ static size_t bar_off(int L) { return dbc_off(L) + (size_t)L * 32 * 4; }
+  // more than half of the SM's shared memory: one block per SM, which the
+  // per-SM checkpoint slots rely on
+  __host__ __device__ static size_t total(int L) {
+    const size_t t = bar_off(L) + 64;
+    return t > 120 * 1024 ? t : 120 * 1024;
+  }
+};
+// checkpoint floats per slot
+__host__ __device__ inline size_t w16_slot_floats(int nck) { return (size_t)(nck > 1 ? nck - 1 : 0) * 16 * kW16Threads; }
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 shfl2(float2 v, int m) {
+  return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
+}
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+template <bool CLAMP>
+__global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams p) {
+  using T = __nv_bfloat16;
+  using Sm = W16Smem;
+  constexpr int K = kW16K;
+  const size_t TILE = Sm::tile_elems();
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint32_t s_tmem_base;
+  __shared__ int s_abort;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int perm = lane & 12;  // register slot j holds state j ^ perm
+  const int pq = perm >> 1;    // the same on state pairs
+  const int L = p.L, D = p.D, S = p.S, nck = p.nck;
+  const int64_t b = blockIdx.x;
+  const int split = blockIdx.y;
+  const int g_begin = split * p.groups_per_cta;
+  const int g_end = min(p.groups, g_begin + p.groups_per_cta);
+  if (g_begin >= g_end) {  // no channels for this split: its dB|dC rows are zero
+    float4* dst = reinterpret_cast<float4*>(p.dBC_ws + ((int64_t)split * p.nseq + b) * L * 32);
+    for (int e = tid; e < L * 8; e += kW16Threads) dst[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const uint32_t slot = smid();
+  if (slot >= (uint32_t)p.ckpt_slots) {  // uniform over the block
+    if (tid == 0) record_error(p.err, HCLSM_ERR_LAUNCH);
+    return;
+  }
+  float4* ckpt = reinterpret_cast<float4*>(p.ckpt_ws + (size_t)slot * w16_slot_floats(nck));
+
+  T* tiles = reinterpret_cast<T*>(smem);
+  float* sBf = reinterpret_cast<float*>(smem + Sm::bc_off());
+  float* sCf = sBf + (size_t)L * 16;
+  float* slab = reinterpret_cast<float*>(smem + Sm::slab_off(L));  // (8, K, 32)
+  float* dbc = reinterpret_cast<float*>(smem + Sm::dbc_off(L));    // (L, 32)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bar_off(L));
+
+  const T* __restrict__ gx = static_cast<const T*>(p.x);
+  const T* __restrict__ gdt = static_cast<const T*>(p.dt);
+  const T* __restrict__ gdy = static_cast<const T*>(p.dy);
+  const T* __restrict__ gz = static_cast<const T*>(p.z);
+  const bool has_z = p.z != nullptr;
+  const bool has_D = p.Dp != nullptr;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    s_abort = 0;
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  {
+    const T* Bm = static_cast<const T*>(p.B) + b * L * S;
+    const T* Cm = static_cast<const T*>(p.C) + b * L * S;
+    for (int i = tid; i < L * 16; i += kW16Threads) {
+      const int t = i >> 4, s = i & 15;
+      sBf[i] = s < S ? __bfloat162float(Bm[(int64_t)t * S + s]) : 0.0f;
+      sCf[i] = s < S ? __bfloat162float(Cm[(int64_t)t * S + s]) : 0.0f;
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 256);
+
+  const int items_per_group = 2 * nck;
+  const int n_items = (g_end - g_begin) * items_per_group;
+  auto issue = [&](int it) {
+    if (it >= n_items) return;
+    const int g = g_begin + it / items_per_group;
+    const int r = it % items_per_group;
+    const bool rev = r >= nck;
+    const int k = rev ? (items_per_group - 1 - r) : r;
+    const int t0 = k * K;
+    const int n = min(K, L - t0);
+    const int c0 = g * kW16Ch;
+    const int w = min(kW16Ch, D - c0);
+    const uint32_t row_bytes = (uint32_t)(w * sizeof(T));
+    const int nten = rev ? (has_z ? 4 : 3) : 2;
+    const int stage = it & 1;
+    T* st = tiles + (size_t)stage * 4 * TILE;
+    if (warp == 0) {
+      if (lane == 0) mbar_expect_tx(&bars[stage], row_bytes * n * nten);
+      __syncwarp();
+      for (int q = lane; q < n * nten; q += 32) {
+        const int ten = q / n, j = q % n;
+        const T* src = ten == 0 ? gx : ten == 1 ? gdt : ten == 2 ? gdy : gz;
+        src += (b * L + t0 + j) * (int64_t)D + c0;
+        bulk_g2s(st + (size_t)ten * TILE + (size_t)j * kW16Ch, src, row_bytes, &bars[stage]);
+      }
+    }
+  };
+  auto wait_item = [&](int it) {
+    if (!s_abort) {
+      if (!mbar_wait(&bars[it & 1], (it >> 1) & 1)) {
+        record_error(p.err, HCLSM_ERR_TIMEOUT);
+        s_abort = 1;
+      }
+    }
+  };
+  issue(0);
+  issue(1);
+
+  // B or C of step t in this lane's slot order: pair q holds states
+  // 2*(q ^ pq) + {0, 1}
+  auto load_bc = [&](const float* base, int t, float2 (&o)[8]) {
+    const float2* row = reinterpret_cast<const float2*>(base + (size_t)t * 16);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = row[q ^ pq];
+  };
+  auto load_ck = [&](int k, float2 (&o)[8]) {  // checkpoint before chunk k (k >= 1)
+    const float4* c = ckpt + (size_t)(k - 1) * 4 * kW16Threads + tid;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = __ldcg(c + (size_t)q * kW16Threads);
+      o[2 * q] = f2(v.x, v.y);
+      o[2 * q + 1] = f2(v.z, v.w);
+    }
+  };
+
+  int it = 0;
+  for (int g = g_begin; g < g_end; ++g) {
+    const int d = g * kW16Ch + tid;
+    const bool act = d < D;
+    float2 A[8];
+    __half2 A2[8];
+    float fac[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int s = j ^ perm;
+      float a = 0.0f, fc = 0.0f;
+      if (act && s < S) {
+        const float e = ex2(p.A_log[(int64_t)d * S + s] * kLog2e);
+        const float ec = CLAMP ? fminf(fmaxf(e, 1e-6f), 1.0f) : e;
+        a = -ec;
+        fc = (CLAMP && (e < 1e-6f || e > 1.0f)) ? 0.0f : -e;
+      }
+      fac[j] = fc;
+      if (j & 1) A[j >> 1].y = a; else A[j >> 1].x = a;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) A2[q] = __floats2half2_rn(A[q].x * kLog2e, A[q].y * kLog2e);
+    const float Dd = (has_D && act) ? p.Dp[d] : 0.0f;
+
+    // ---- forward sweep: checkpoints (to this SM's L2-resident slot) ------------
+    float2 h[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) h[q] = f2(0.0f, 0.0f);
+    for (int k = 0; k < nck; ++k, ++it) {
+      wait_item(it);
+      const T* st = tiles + (size_t)(it & 1) * 4 * TILE + tid;
+      const int t0 = k * K, n = min(K, L - t0);
+      if (k > 0) {
+        float4* c = ckpt + (size_t)(k - 1) * 4 * kW16Threads + tid;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          __stcg(c + (size_t)q * kW16Threads, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y));
+      }
+#pragma unroll 2
+      for (int j = 0; j < n; ++j) {
+        const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
+        float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
+        const float2 dtx = f2(dv * xv, dv * xv);
+        const __half2 dth = __float2half2_rn(dv);
+        float2 Bt[8];
+        load_bc(sBf, t0 + j, Bt);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float2 dA = __half22float2(ex2_h2(__hmul2(dth, A2[q])));
+          h[q] = __ffma2_rn(dA, h[q], __fmul2_rn(dtx, Bt[q]));
+        }
+      }
+      __syncthreads();
+      if (warp == 0) issue(it + 2);
+    }
+
+    // ---- reverse sweep --------------------------------------------------------
+    float2 gcar[8], gAcc[8], hk[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) { gcar[q] = f2(0.0f, 0.0f); gAcc[q] = f2(0.0f, 0.0f); }
+    float dDacc = 0.0f;
+    if (nck > 1) {
+      load_ck(nck - 1, hk);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) hk[q] = f2(0.0f, 0.0f);
+    }
+    for (int k = nck - 1; k >= 0; --k, ++it) {
+      wait_item(it);
+      const T* st = tiles + (size_t)(it & 1) * 4 * TILE + tid;
+      const int t0 = k * K, n = min(K, L - t0);
+      float2 hs[8], hnext[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) hs[q] = hk[q];
+      // fetch the previous chunk's checkpoint while this chunk runs
+      if (k > 1) {
+        load_ck(k - 1, hnext);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hnext[q] = f2(0.0f, 0.0f);
+      }
+      // recompute the chunk: h_t (fp32) and dA_t (f16 pairs) into TMEM
+#pragma unroll 2
+      for (int j = 0; j < n; ++j) {
+        const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
+        float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
+        const float2 dtx = f2(dv * xv, dv * xv);
+        const __half2 dth = __float2half2_rn(dv);
+        float2 Bt[8];
+        load_bc(sBf, t0 + j, Bt);
+        float hv[16], dw[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const __half2 e = ex2_h2(__hmul2(dth, A2[q]));
+          hs[q] = __ffma2_rn(__half22float2(e), hs[q], __fmul2_rn(dtx, Bt[q]));
+          hv[2 * q] = hs[q].x;
+          hv[2 * q + 1] = hs[q].y;
+          dw[q] = __uint_as_float(h2_bits(e));
+        }
+        const uint32_t col = tmem + (uint32_t)(j * kW16Cols);
+        tmem_st16(col, hv);
+        tmem_st8(col + 16, dw);
+      }
+      tmem_wait_st();
+      float nh[16], nd[8];
+      {
+        const uint32_t col = tmem + (uint32_t)((n - 1) * kW16Cols);
+        tmem_ld8(col + 16, nd);
+        if (n - 1 > 0) tmem_ld16(col - kW16Cols, nh);
+      }
+#pragma unroll 2
+      for (int j = n - 1; j >= 0; --j) {
+        const int t = t0 + j;
+        tmem_wait_ld();
+        float2 hp[8];
+        uint32_t dwv[8];
+        if (j > 0) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) hp[q] = f2(nh[2 * q], nh[2 * q + 1]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) hp[q] = hk[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dwv[q] = __float_as_uint(nd[q]);
+        if (j > 0) {
+          const uint32_t col = tmem + (uint32_t)((j - 1) * kW16Cols);
+          tmem_ld8(col + 16, nd);
+          if (j - 1 > 0) tmem_ld16(col - kW16Cols, nh);
+        }
+        const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
+        const float draw = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        float gy = act ? __bfloat162float(st[2 * TILE + (size_t)j * kW16Ch]) : 0.0f;
+        float dv = draw, mdt = 1.0f;
+        if (CLAMP) {
+          mdt = (draw >= 1e-3f && draw <= 1.0f) ? 1.0f : 0.0f;
+          dv = fminf(fmaxf(draw, 1e-3f), 1.0f);
+        }
+        const float dtxs = dv * xv;
+        float2 Bt[8], Ct[8];
+        load_bc(sBf, t, Bt);
+        load_bc(sCf, t, Ct);
+        float dzv = 0.0f;
+        if (has_z) {
+          const float zv = act ? __bfloat162float(st[3 * TILE + (size_t)j * kW16Ch]) : 0.0f;
+          float2 ys2 = f2(0.0f, 0.0f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) ys2 = __ffma2_rn(hs[q], Ct[q], ys2);
+          const float ys = fmaf(Dd, xv, ys2.x + ys2.y);
+          const float sg = sigmoid(zv);
+          dzv = gy * ys * sg * (1.0f + zv * (1.0f - sg));
+          gy = gy * zv * sg;
+        }
+        const float2 gyy = f2(gy, gy), dtx = f2(dtxs, dtxs), dvv = f2(dv, dv);
+        float2 gB = f2(0.0f, 0.0f), ddA = f2(0.0f, 0.0f);
+        float2 v[16];  // (dB, dC) partials per register slot
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float2 gs = __ffma2_rn(gyy, Ct[q], gcar[q]);
+          gB = __ffma2_rn(gs, Bt[q], gB);
+          const float2 pB = __fmul2_rn(gs, dtx);
+          const float2 pC = __fmul2_rn(gyy, hs[q]);
+          v[2 * q] = f2(pB.x, pC.x);
+          v[2 * q + 1] = f2(pB.y, pC.y);
+          const float2 w = __fmul2_rn(__half22float2(bits_h2(dwv[q])), gs);
+          const float2 R = __fmul2_rn(w, hp[q]);
+          ddA = __ffma2_rn(A[q], R, ddA);
+          gAcc[q] = __ffma2_rn(dvv, R, gAcc[q]);
+          gcar[q] = w;
+          hs[q] = hp[q];
+        }
+        dDacc = fmaf(gy, xv, dDacc);
+        if (act) {
+          const int64_t gi = (b * L + t) * (int64_t)D + d;
+          const float gBs = gB.x + gB.y;
+          static_cast<T*>(p.dx)[gi] = __float2bfloat16_rn(fmaf(dv, gBs, Dd * gy));
+          static_cast<T*>(p.ddt)[gi] = __float2bfloat16_rn(fmaf(xv, gBs, ddA.x + ddA.y) * mdt);
+          if (has_z) static_cast<T*>(p.dz)[gi] = __float2bfloat16_rn(dzv);
+        }
+        // reduce (dB, dC) over the warp's 32 channels
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fadd2_rn(v[i], shfl2(v[i + 8], 8));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fadd2_rn(v[i], shfl2(v[i + 4], 4));
+        {
+          const bool up = (lane & 2) != 0;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const float2 snd = up ? v[i] : v[i + 2];
+            const float2 kp = up ? v[i + 2] : v[i];
+            v[i] = __fadd2_rn(kp, shfl2(snd, 2));
+          }
+        }
+        {
+          const bool up = (lane & 1) != 0;
+          const float2 snd = up ? v[0] : v[1];
+          const float2 kp = up ? v[1] : v[0];
+          v[0] = __fadd2_rn(kp, shfl2(snd, 1));
+        }
+        v[0] = __fadd2_rn(v[0], shfl2(v[0], 16));
+        // lane l holds the warp totals of state (l & 15): dB in .x, dC in .y
+        slab[((size_t)warp * K + j) * 32 + lane] = lane < 16 ? v[0].x : v[0].y;
+      }
+      __syncthreads();
+      {
+        const bool first = (g == g_begin);
+        for (int e = tid; e < n * 32; e += kW16Threads) {
+          const int j = e >> 5, vv = e & 31;
+          float acc = 0.0f;
+#pragma unroll
+          for (int w8 = 0; w8 < 8; ++w8) acc += slab[((size_t)w8 * K + j) * 32 + vv];
+          float* dst = dbc + (size_t)t0 * 32 + e;
+          *dst = first ? acc : *dst + acc;
+        }
+      }
+      __syncthreads();
+      if (warp == 0) issue(it + 2);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) hk[q] = hnext[q];
+    }
+    if (act) {
+      float* da = p.dAlog_part + (b * D + d) * (int64_t)S;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int s = j ^ perm;
+        const float gv = (j & 1) ? gAcc[j >> 1].y : gAcc[j >> 1].x;
+        if (s < S) da[s] = gv * fac[j];
+      }
+      if (has_D) p.dD_part[b * D + d] = dDacc;
+    }
+  }
+  // this sequence's dB | dC rows (the last fold ended with a barrier)
+  {
+    float4* dst = reinterpret_cast<float4*>(p.dBC_ws + ((int64_t)split * p.nseq + b) * L * 32);
+    const float4* src = reinterpret_cast<const float4*>(dbc);
+    for (int e = tid; e < L * 8; e += kW16Threads) dst[e] = src[e];
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(s_tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 // out[c] = sum_r part[r][c] over `rows` rows, deterministic (fixed order).
 // Stage 1 sums row blocks of `rb` rows into part2[blk][c].
 __global__ void colsum_stage1(const float* __restrict__ part, float* __restrict__ part2, int64_t rows,
@@ -884,9 +1313,9 @@ static int launch_fwd(const FwdParams& p, bool clamp, cudaStream_t st) {
 
 // ---- backward plan -----------------------------------------------------------
 struct BwdPlan {
-  int SP, K, nck, groups, nsplit, gpc;
+  int SP, K, nck, groups, nsplit, gpc, nck16, slots;
   int64_t nblk, rb;
-  size_t off_dalog, off_dd, off_p2a, off_p2d, off_dbc, total;
+  size_t off_dalog, off_dd, off_p2a, off_p2d, off_dbc, off_ck, total;
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -930,6 +1359,10 @@ static bool plan_bwd(int64_t nseq, int L, int D, int S, BwdPlan* pl) {
   pl->off_p2a = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D * S);
   pl->off_p2d = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D);
   pl->off_dbc = off;   off = align256(off + sizeof(float) * (size_t)pl->nsplit * nseq * L * 2 * SP);
+  // checkpoint slots of the packed bf16 kernel (d_state 9..16), one per SM
+  pl->nck16 = (L + kW16K - 1) / kW16K;
+  pl->slots = SP == 16 ? std::min(nsm, kW16MaxSlots) : 0;
+  pl->off_ck = off;    off = align256(off + sizeof(float) * (size_t)pl->slots * w16_slot_floats(pl->nck16));
   pl->total = off;
   return true;
 }
@@ -944,8 +1377,26 @@ static int launch_bwd_t(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) 
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
 }
 
+template <bool CLAMP>
+static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) {
+  const size_t smem = W16Smem::total(p.L);
+  if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
+  BwdParams q = p;
+  q.nck = pl.nck16;
+  q.groups = (p.D + kW16Ch - 1) / kW16Ch;
+  // the channel split of the plan counts 128-channel groups; keep its CTA count
+  q.groups_per_cta = (q.groups + pl.nsplit - 1) / pl.nsplit;
+  auto fn = scan_bwd_bf16_kernel<CLAMP>;
+  if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
+  fn<<<dim3((unsigned)p.nseq, pl.nsplit), kW16Threads, smem, st>>>(q);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
 template <typename T>
 static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (pl.SP == 16) return clamp ? launch_bwd_bf16<true>(p, pl, st) : launch_bwd_bf16<false>(p, pl, st);
+  }
   switch (pl.SP) {
     case 4: return clamp ? launch_bwd_t<T, 4, true>(p, pl, st) : launch_bwd_t<T, 4, false>(p, pl, st);
     case 8: return clamp ? launch_bwd_t<T, 8, true>(p, pl, st) : launch_bwd_t<T, 8, false>(p, pl, st);
@@ -1017,6 +1468,8 @@ extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_
   p.dBC_ws = reinterpret_cast<float*>(ws + pl.off_dbc);
   p.nseq = nseq; p.L = L; p.D = d_inner; p.S = d_state;
   p.nck = pl.nck; p.groups = pl.groups; p.groups_per_cta = pl.gpc; p.nsplit = pl.nsplit;
+  p.ckpt_ws = reinterpret_cast<float*>(ws + pl.off_ck);
+  p.ckpt_slots = pl.slots;
   p.err = device_err_ptr();
   int rc = dtype == HCLSM_F32 ? launch_bwd<float>(p, pl, clamp != 0, st)
                               : launch_bwd<__nv_bfloat16>(p, pl, clamp != 0, st);
