@@ -777,7 +777,7 @@ struct W16Smem {
   __host__ __device__ static size_t tiles_bytes() { return 2 * 4 * tile_elems() * 2; }
   __host__ __device__ static size_t bc_off() { return tiles_bytes(); }
   __host__ __device__ static size_t slab_off(int L) { return bc_off() + (size_t)L * 16 * 2 * 4; }
-  __host__ __device__ static size_t dbc_off(int L) { return slab_off(L) + 8 * (size_t)kW16K * 32 * 4; }
+  __host__ __device__ static size_t dbc_off(int L) { return slab_off(L) + 2 * 8 * (size_t)kW16K * 32 * 4; }
   __host__ __device__ static size_t bar_off(int L) { return dbc_off(L) + (size_t)L * 32 * 4; }
   // more than half of the SM's shared memory: one block per SM, which the
   // per-SM checkpoint slots rely on
@@ -830,11 +830,14 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     return;
   }
   float4* ckpt = reinterpret_cast<float4*>(p.ckpt_ws + (size_t)slot * w16_slot_floats(nck));
+  // checkpoints stay in L2; the streamed inputs should not displace them
+  const uint64_t keep = policy_evict_last(), stream_pol = policy_evict_first();
 
   T* tiles = reinterpret_cast<T*>(smem);
   float* sBf = reinterpret_cast<float*>(smem + Sm::bc_off());
   float* sCf = sBf + (size_t)L * 16;
-  float* slab = reinterpret_cast<float*>(smem + Sm::slab_off(L));  // (8, K, 32)
+  float* slab0 = reinterpret_cast<float*>(smem + Sm::slab_off(L));  // 2 x (8, K, 32)
+  int slab_buf = 0;
   float* dbc = reinterpret_cast<float*>(smem + Sm::dbc_off(L));    // (L, 32)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bar_off(L));
 
@@ -895,7 +898,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         const int ten = q / n, j = q % n;
         const T* src = ten == 0 ? gx : ten == 1 ? gdt : ten == 2 ? gdy : gz;
         src += (b * L + t0 + j) * (int64_t)D + c0;
-        bulk_g2s(st + (size_t)ten * TILE + (size_t)j * kW16Ch, src, row_bytes, &bars[stage]);
+        bulk_g2s_hint(st + (size_t)ten * TILE + (size_t)j * kW16Ch, src, row_bytes, &bars[stage], stream_pol);
       }
     }
   };
@@ -921,7 +924,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     const float4* c = ckpt + (size_t)(k - 1) * 4 * kW16Threads + tid;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float4 v = __ldcg(c + (size_t)q * kW16Threads);
+      const float4 v = ld_hint(c + (size_t)q * kW16Threads, keep);
       o[2 * q] = f2(v.x, v.y);
       o[2 * q + 1] = f2(v.z, v.w);
     }
@@ -963,7 +966,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         float4* c = ckpt + (size_t)(k - 1) * 4 * kW16Threads + tid;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          __stcg(c + (size_t)q * kW16Threads, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y));
+          st_hint(c + (size_t)q * kW16Threads, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y), keep);
       }
 #pragma unroll 2
       for (int j = 0; j < n; ++j) {
@@ -999,6 +1002,8 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       wait_item(it);
       const T* st = tiles + (size_t)(it & 1) * 4 * TILE + tid;
       const int t0 = k * K, n = min(K, L - t0);
+      float* slab = slab0 + (size_t)slab_buf * 8 * K * 32;
+      slab_buf ^= 1;
       float2 hs[8], hnext[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) hs[q] = hk[q];
@@ -1144,7 +1149,8 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
           *dst = first ? acc : *dst + acc;
         }
       }
-      __syncthreads();
+      // no barrier here: the next chunk writes the other slab buffer, and the
+      // barrier that ends it orders these folds before this buffer is reused
       if (warp == 0) issue(it + 2);
 #pragma unroll
       for (int q = 0; q < 8; ++q) hk[q] = hnext[q];
@@ -1160,7 +1166,8 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       if (has_D) p.dD_part[b * D + d] = dDacc;
     }
   }
-  // this sequence's dB | dC rows (the last fold ended with a barrier)
+  __syncthreads();
+  // this sequence's dB | dC rows
   {
     float4* dst = reinterpret_cast<float4*>(p.dBC_ws + ((int64_t)split * p.nseq + b) * L * 32);
     const float4* src = reinterpret_cast<const float4*>(dbc);
