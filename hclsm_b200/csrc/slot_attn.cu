@@ -1,0 +1,500 @@
+// Slot attention for B200 (sm_100a): the attention core and the fused
+// element-wise stages of DynamicSlotAttention._iteration_step.
+//
+// Reference semantics (paths inside RightNow-AI/hclsm):
+//   hclsm/kernels/slot_attention_kernel.py:265-291 naive_slot_attention:
+//       logits = Q K^T * scale ; attn = softmax over the SLOT axis ; out = attn V
+//   :126 (Triton pass 2) adds 1e-8 to the softmax denominator (eps argument);
+//   hclsm/objects/dynamic_slots.py:98-131 _iteration_step clamps the logits to
+//   [-30, 30] (clamp argument), then GRUCell, residual MLP, clamp to [-50, 50].
+//
+// Attention core, bf16 path: one CTA (8 warps) per frame.  Tokens are processed
+// in chunks of 64; each chunk's K and V rows arrive in shared memory through
+// 1-D bulk copies (TMA engine) on an mbarrier.  Phase 1 (4 warps, 16 tokens
+// each): logits = K_tile * Q^T on tensor cores (mma.sync m16n8k16, bf16 in,
+// fp32 accumulate); each token's softmax over the slots is a reduction inside
+// a lane quad.  Phase 2 (8 warps, D split in 8-column tiles): out += attn^T-tile
+// * V on tensor cores, fp32 accumulators in registers across chunks.  Padded
+// slots are masked to -inf (they do not join the softmax) and padded tokens
+// get zero weight.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace hclsm {
+int* device_err_ptr();
+bool set_smem_limit(const void* fn, size_t bytes);
+}  // namespace hclsm
+
+namespace hclsm {
+namespace slot {
+
+constexpr int kThreads = 256;
+constexpr int kChunk = 64;   // tokens per chunk
+constexpr int kPad = 8;      // bf16 elements of row padding (16 B): conflict-free ldmatrix
+
+struct CoreParams {
+  const void* Q;  // (F, N, D)
+  const void* K;  // (F, M, D)
+  const void* V;  // (F, M, D)
+  void* out;      // (F, N, D)
+  void* attn;     // (F, N, M) or null
+  int F, N, M, D;
+  float scale, clamp, eps;
+  int attn_f32;  // attn stored as fp32 (1) or in the I/O dtype (0)
+  int* err;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared memory: Q (NP rows), K chunk, V chunk (kChunk rows each, row stride
+// D + kPad), attn chunk [NP][kChunk + kPad], one mbarrier.
+struct CoreSmem {
+  static __host__ __device__ size_t row(int D) { return (size_t)(D + kPad) * 2; }
+  static __host__ __device__ size_t q_off() { return 0; }
+  static __host__ __device__ size_t k_off(int NP, int D) { return q_off() + NP * row(D); }
+  static __host__ __device__ size_t v_off(int NP, int D) { return k_off(NP, D) + kChunk * row(D); }
+  static __host__ __device__ size_t a_off(int NP, int D) { return v_off(NP, D) + kChunk * row(D); }
+  static __host__ __device__ size_t bar_off(int NP, int D) { return a_off(NP, D) + (size_t)NP * (kChunk + kPad) * 2; }
+  static __host__ __device__ size_t total(int NP, int D) { return bar_off(NP, D) + 16; }
+};
+
+// NM: 16-slot tiles (N <= 16*NM); NT: 8-column output tiles per warp (D <= 64*NT)
+template <int NM, int NT>
+__global__ void __launch_bounds__(kThreads, 1) core_bf16_kernel(CoreParams p) {
+  constexpr int NP = 16 * NM;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int f = blockIdx.x;
+  const int N = p.N, M = p.M, D = p.D;
+  const size_t RB = CoreSmem::row(D);
+  unsigned char* sQ = smem + CoreSmem::q_off();
+  unsigned char* sK = smem + CoreSmem::k_off(NP, D);
+  unsigned char* sV = smem + CoreSmem::v_off(NP, D);
+  __nv_bfloat16* sA = reinterpret_cast<__nv_bfloat16*>(smem + CoreSmem::a_off(NP, D));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + CoreSmem::bar_off(NP, D));
+  const __nv_bfloat16* gQ = static_cast<const __nv_bfloat16*>(p.Q) + (size_t)f * N * D;
+  const __nv_bfloat16* gK = static_cast<const __nv_bfloat16*>(p.K) + (size_t)f * M * D;
+  const __nv_bfloat16* gV = static_cast<const __nv_bfloat16*>(p.V) + (size_t)f * M * D;
+  const uint32_t row_bytes = (uint32_t)D * 2;
+
+  // Q rows (padded slots zero) through the bulk engine, together with chunk 0
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < (NP - N) * (D + kPad); i += kThreads)
+    reinterpret_cast<__nv_bfloat16*>(sQ + (size_t)N * RB)[i] = __float2bfloat16_rn(0.0f);
+  __syncthreads();
+  auto issue_chunk = [&](int m0, bool with_q) {
+    const int rows = min(kChunk, M - m0);
+    if (warp == 0) {
+      if (lane == 0)
+        mbar_expect_tx(bar, row_bytes * (2 * rows + (with_q ? N : 0)));
+      __syncwarp();
+      for (int r = lane; r < rows; r += 32) {
+        bulk_g2s(sK + (size_t)r * RB, gK + (size_t)(m0 + r) * D, row_bytes, bar);
+        bulk_g2s(sV + (size_t)r * RB, gV + (size_t)(m0 + r) * D, row_bytes, bar);
+      }
+      if (with_q)
+        for (int r = lane; r < N; r += 32) bulk_g2s(sQ + (size_t)r * RB, gQ + (size_t)r * D, row_bytes, bar);
+    }
+  };
+  issue_chunk(0, true);
+
+  float acc[NM][NT][4];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int b = 0; b < NT; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.0f;
+
+  const int g = lane >> 2, t4 = lane & 3;
+  const float sc = p.scale;
+  const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV), sAa = smem_u32(sA);
+  constexpr int AR = kChunk + kPad;  // attn row stride (elements)
+  int phase = 0;
+  for (int m0 = 0; m0 < M; m0 += kChunk) {
+    const int rows = min(kChunk, M - m0);
+    if (!mbar_wait(bar, phase)) record_error(p.err, HCLSM_ERR_TIMEOUT);
+    phase ^= 1;
+    // zero K/V rows past the end of the token range
+    if (rows < kChunk) {
+      for (int i = tid; i < (kChunk - rows) * (D / 2); i += kThreads) {
+        const int r = rows + i / (D / 2), c = i % (D / 2);
+        reinterpret_cast<uint32_t*>(sK + (size_t)r * RB)[c] = 0u;
+        reinterpret_cast<uint32_t*>(sV + (size_t)r * RB)[c] = 0u;
+      }
+      __syncthreads();
+    }
+    // ---- phase 1: logits for 16 tokens x NP slots per warp ---------------------
+    if (warp < kChunk / 16) {
+      const int tk0 = warp * 16;
+      float lg[2 * NM][4];
+#pragma unroll
+      for (int a = 0; a < 2 * NM; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) lg[a][c] = 0.0f;
+      for (int k0 = 0; k0 < D; k0 += 16) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(sKa + (uint32_t)((tk0 + (lane & 15)) * RB + (k0 + (lane >> 4) * 8) * 2), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < 2 * NM; ++nt) {
+          uint32_t b0, b1;
+          ldsm_x2(sQa + (uint32_t)((nt * 8 + (lane & 7)) * RB + (k0 + ((lane >> 3) & 1) * 8) * 2), b0, b1);
+          mma_bf16(lg[nt], a0, a1, a2, a3, b0, b1);
+        }
+      }
+      // rows g (c0, c1) and g+8 (c2, c3); columns (slots) nt*8 + 2*t4 + {0,1}
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2 * NM; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int s = nt * 8 + 2 * t4 + e;
+            float v = lg[nt][2 * hrow + e] * sc;
+            if (p.clamp > 0.0f) v = fminf(fmaxf(v, -p.clamp), p.clamp);
+            v = s < N ? v : -INFINITY;
+            lg[nt][2 * hrow + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        float sum = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 2 * NM; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float ev = ex2((lg[nt][2 * hrow + e] - mx) * kLog2e);
+            lg[nt][2 * hrow + e] = ev;
+            sum += ev;
+          }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const float inv = 1.0f / (sum + p.eps);
+        const int tok = tk0 + g + 8 * hrow;
+        const bool tv = tok < rows;
+#pragma unroll
+        for (int nt = 0; nt < 2 * NM; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int s = nt * 8 + 2 * t4 + e;
+            const float a = tv ? lg[nt][2 * hrow + e] * inv : 0.0f;
+            sA[s * AR + tok] = __float2bfloat16_rn(a);
+            if (p.attn && tv && s < N) {
+              const size_t gi = ((size_t)f * N + s) * M + m0 + tok;
+              if (p.attn_f32) static_cast<float*>(p.attn)[gi] = a;
+              else static_cast<__nv_bfloat16*>(p.attn)[gi] = __float2bfloat16_rn(a);
+            }
+          }
+      }
+    }
+    __syncthreads();
+    // ---- phase 2: out += attn^T * V for this warp's column tiles ---------------
+    for (int k0 = 0; k0 < kChunk; k0 += 16) {
+      uint32_t af[NM][4];
+#pragma unroll
+      for (int mt = 0; mt < NM; ++mt)
+        ldsm_x4(sAa + (uint32_t)(((mt * 16 + (lane & 15)) * AR + k0 + (lane >> 4) * 8) * 2), af[mt][0], af[mt][1],
+                af[mt][2], af[mt][3]);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int n0 = (warp + 8 * j) * 8;
+        if (n0 < D) {
+          uint32_t b0, b1;
+          ldsm_x2_t(sVa + (uint32_t)((k0 + (lane & 15)) * RB + n0 * 2), b0, b1);
+#pragma unroll
+          for (int mt = 0; mt < NM; ++mt) mma_bf16(acc[mt][j], af[mt][0], af[mt][1], af[mt][2], af[mt][3], b0, b1);
+        }
+      }
+    }
+    __syncthreads();
+    if (m0 + kChunk < M) issue_chunk(m0 + kChunk, false);
+  }
+  // ---- epilogue -------------------------------------------------------------------
+  __nv_bfloat16* gO = static_cast<__nv_bfloat16*>(p.out) + (size_t)f * N * D;
+#pragma unroll
+  for (int mt = 0; mt < NM; ++mt)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int n0 = (warp + 8 * j) * 8;
+      if (n0 < D) {
+        const int r0 = mt * 16 + g, c = n0 + 2 * t4;
+        if (r0 < N)
+          *reinterpret_cast<__nv_bfloat162*>(gO + (size_t)r0 * D + c) = __floats2bfloat162_rn(acc[mt][j][0], acc[mt][j][1]);
+        if (r0 + 8 < N)
+          *reinterpret_cast<__nv_bfloat162*>(gO + (size_t)(r0 + 8) * D + c) =
+              __floats2bfloat162_rn(acc[mt][j][2], acc[mt][j][3]);
+      }
+    }
+}
+
+// fp32 I/O path on CUDA cores (exact fp32 arithmetic), one CTA per frame.
+constexpr int kF32Chunk = 64;
+__global__ void __launch_bounds__(kThreads) core_f32_kernel(CoreParams p) {
+  extern __shared__ __align__(16) float fsm[];  // logits/attn chunk [N][kF32Chunk]
+  const int f = blockIdx.x, tid = threadIdx.x;
+  const int N = p.N, M = p.M, D = p.D;
+  const float* Q = static_cast<const float*>(p.Q) + (size_t)f * N * D;
+  const float* K = static_cast<const float*>(p.K) + (size_t)f * M * D;
+  const float* V = static_cast<const float*>(p.V) + (size_t)f * M * D;
+  float* O = static_cast<float*>(p.out) + (size_t)f * N * D;
+  for (int i = tid; i < N * D; i += kThreads) O[i] = 0.0f;
+  for (int m0 = 0; m0 < M; m0 += kF32Chunk) {
+    const int rows = min(kF32Chunk, M - m0);
+    __syncthreads();
+    for (int i = tid; i < N * rows; i += kThreads) {
+      const int s = i / rows, m = i % rows;
+      const float* q = Q + (size_t)s * D;
+      const float* k = K + (size_t)(m0 + m) * D;
+      float a = 0.0f;
+      for (int d = 0; d < D; ++d) a = fmaf(q[d], k[d], a);
+      a *= p.scale;
+      if (p.clamp > 0.0f) a = fminf(fmaxf(a, -p.clamp), p.clamp);
+      fsm[s * kF32Chunk + m] = a;
+    }
+    __syncthreads();
+    for (int m = tid; m < rows; m += kThreads) {
+      float mx = -INFINITY;
+      for (int s = 0; s < N; ++s) mx = fmaxf(mx, fsm[s * kF32Chunk + m]);
+      float sum = 0.0f;
+      for (int s = 0; s < N; ++s) {
+        const float e = expf(fsm[s * kF32Chunk + m] - mx);
+        fsm[s * kF32Chunk + m] = e;
+        sum += e;
+      }
+      const float inv = 1.0f / (sum + p.eps);
+      for (int s = 0; s < N; ++s) {
+        const float a = fsm[s * kF32Chunk + m] * inv;
+        fsm[s * kF32Chunk + m] = a;
+        if (p.attn) static_cast<float*>(p.attn)[((size_t)f * N + s) * M + m0 + m] = a;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < N * D; i += kThreads) {
+      const int s = i / D, d = i % D;
+      float a = 0.0f;
+      for (int m = 0; m < rows; ++m) a = fmaf(fsm[s * kF32Chunk + m], V[(size_t)(m0 + m) * D + d], a);
+      O[i] += a;
+    }
+  }
+}
+
+// ---- fused element-wise stages ----------------------------------------------------
+// y = LayerNorm(x) * w + b over the last dimension (one warp per row); x fp32,
+// y in bf16 (GEMM operand) or fp32.
+template <typename TO>
+__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                 const float* __restrict__ b, TO* __restrict__ y, int64_t rows, int D, float eps) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* xr = x + r * D;
+  float s = 0.0f;
+  for (int i = lane; i < D; i += 32) s += xr[i];
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+  const float mu = s / D;
+  float v = 0.0f;
+  for (int i = lane; i < D; i += 32) {
+    const float t = xr[i] - mu;
+    v += t * t;
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  const float rs = rsqrtf(v / D + eps);
+  for (int i = lane; i < D; i += 32) {
+    float o = (xr[i] - mu) * rs;
+    if (w) o *= w[i];
+    if (b) o += b[i];
+    io<TO>::st(y + r * D + i, o);
+  }
+}
+
+// torch.nn.GRUCell: gate rows ordered (r, z, n).  gi = x W_ih^T, gh = h W_hh^T
+// (fp32, without biases); h_out = (1 - z) * n + z * h.
+__global__ void gru_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
+                           const float* __restrict__ b_ih, const float* __restrict__ b_hh,
+                           const float* __restrict__ h, float* __restrict__ h_out, int64_t rows, int H) {
+  const int64_t total = rows * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H;
+    const int c = (int)(i % H);
+    const float* gir = gi + r * 3 * H;
+    const float* ghr = gh + r * 3 * H;
+    const float rg = sigmoid(gir[c] + b_ih[c] + ghr[c] + b_hh[c]);
+    const float zg = sigmoid(gir[H + c] + b_ih[H + c] + ghr[H + c] + b_hh[H + c]);
+    const float pre = gir[2 * H + c] + b_ih[2 * H + c] + rg * (ghr[2 * H + c] + b_hh[2 * H + c]);
+    const float ng = 2.0f * sigmoid(2.0f * pre) - 1.0f;  // tanh
+    h_out[i] = (1.0f - zg) * ng + zg * h[i];
+  }
+}
+
+// y = act(x + b) for a (rows, C) fp32 matrix; act 0 = identity, 1 = ReLU.
+template <typename TO>
+__global__ void bias_act_kernel(const float* __restrict__ x, const float* __restrict__ b, TO* __restrict__ y,
+                                int64_t rows, int C, int act) {
+  const int64_t total = rows * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = x[i] + (b ? b[i % C] : 0.0f);
+    if (act == 1) v = fmaxf(v, 0.0f);
+    io<TO>::st(y + i, v);
+  }
+}
+
+// out = clamp(h + m + b, -c, c) (fp32), plus an optional bf16 copy.
+__global__ void residual_clamp_kernel(const float* __restrict__ h, const float* __restrict__ m,
+                                      const float* __restrict__ b, float* __restrict__ out,
+                                      __nv_bfloat16* __restrict__ out_bf16, int64_t rows, int C, float c) {
+  const int64_t total = rows * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = h[i] + m[i] + (b ? b[i % C] : 0.0f);
+    if (c > 0.0f) v = fminf(fmaxf(v, -c), c);
+    out[i] = v;
+    if (out_bf16) out_bf16[i] = __float2bfloat16_rn(v);
+  }
+}
+
+}  // namespace slot
+}  // namespace hclsm
+
+using namespace hclsm;
+using namespace hclsm::slot;
+
+template <int NM, int NT>
+static int launch_core_bf16(const CoreParams& p, cudaStream_t st) {
+  const size_t smem = CoreSmem::total(16 * NM, p.D);
+  if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
+  auto fn = core_bf16_kernel<NM, NT>;
+  if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
+  fn<<<p.F, kThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+template <int NM>
+static int launch_core_nm(const CoreParams& p, cudaStream_t st) {
+  const int nt = (p.D + 63) / 64;
+  switch (nt) {
+    case 1: return launch_core_bf16<NM, 1>(p, st);
+    case 2: return launch_core_bf16<NM, 2>(p, st);
+    case 3: return launch_core_bf16<NM, 3>(p, st);
+    case 4: return launch_core_bf16<NM, 4>(p, st);
+    case 5: return launch_core_bf16<NM, 5>(p, st);
+    case 6: return launch_core_bf16<NM, 6>(p, st);
+    case 7: return launch_core_bf16<NM, 7>(p, st);
+    case 8: return launch_core_bf16<NM, 8>(p, st);
+  }
+  return HCLSM_ERR_UNSUPPORTED;
+}
+
+extern "C" int hclsm_slot_attn_core(const void* Q, const void* K, const void* V, void* out, void* attn,
+                                    int32_t F, int32_t N, int32_t M, int32_t D, float scale, float clamp,
+                                    float eps, int32_t dtype, int32_t attn_f32, void* stream) {
+  if (!Q || !K || !V || !out) return HCLSM_ERR_NULL;
+  if (F < 0 || N <= 0 || M < 0 || D <= 0) return HCLSM_ERR_SHAPE;
+  if (F == 0) return HCLSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CoreParams p{Q, K, V, out, attn, F, N, M, D, scale, clamp, eps, attn_f32, device_err_ptr()};
+  if (M == 0) {
+    cudaMemsetAsync(out, 0, (size_t)F * N * D * (dtype == HCLSM_F32 ? 4 : 2), st);
+    return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  }
+  if (dtype == HCLSM_F32) {
+    if (attn && !attn_f32) return HCLSM_ERR_DTYPE;
+    const size_t smem = (size_t)N * kF32Chunk * sizeof(float);
+    if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
+    if (!set_smem_limit(reinterpret_cast<const void*>(core_f32_kernel), smem)) return HCLSM_ERR_LAUNCH;
+    core_f32_kernel<<<F, kThreads, smem, st>>>(p);
+    return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  }
+  if (dtype != HCLSM_BF16) return HCLSM_ERR_DTYPE;
+  // bulk copies and ldmatrix rows need 16-byte rows
+  if (D % 16 != 0 || D > 512 || N > 64) return HCLSM_ERR_UNSUPPORTED;
+  auto al = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (!al(Q) || !al(K) || !al(V) || !al(out)) return HCLSM_ERR_ALIGN;
+  switch ((N + 15) / 16) {
+    case 1: return launch_core_nm<1>(p, st);
+    case 2: return launch_core_nm<2>(p, st);
+    case 3: return launch_core_nm<3>(p, st);
+    case 4: return launch_core_nm<4>(p, st);
+  }
+  return HCLSM_ERR_UNSUPPORTED;
+}
+
+static unsigned ew_blocks(int64_t n) {
+  int64_t b = (n + 255) / 256;
+  return (unsigned)(b < 148 * 32 ? (b > 0 ? b : 1) : 148 * 32);
+}
+
+extern "C" int hclsm_layernorm(const float* x, const float* w, const float* b, void* y, int64_t rows, int32_t D,
+                               float eps, int32_t out_dtype, void* stream) {
+  if (!x || !y) return HCLSM_ERR_NULL;
+  if (rows < 0 || D <= 0) return HCLSM_ERR_SHAPE;
+  if (rows == 0) return HCLSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (out_dtype == HCLSM_BF16)
+    layernorm_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(x, w, b, static_cast<__nv_bfloat16*>(y), rows, D, eps);
+  else if (out_dtype == HCLSM_F32)
+    layernorm_kernel<float><<<blocks, 256, 0, st>>>(x, w, b, static_cast<float*>(y), rows, D, eps);
+  else
+    return HCLSM_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+extern "C" int hclsm_gru_cell(const float* gi, const float* gh, const float* b_ih, const float* b_hh,
+                              const float* h, float* h_out, int64_t rows, int32_t H, void* stream) {
+  if (!gi || !gh || !b_ih || !b_hh || !h || !h_out) return HCLSM_ERR_NULL;
+  if (rows < 0 || H <= 0) return HCLSM_ERR_SHAPE;
+  if (rows == 0) return HCLSM_OK;
+  gru_kernel<<<ew_blocks(rows * H), 256, 0, static_cast<cudaStream_t>(stream)>>>(gi, gh, b_ih, b_hh, h, h_out,
+                                                                                 rows, H);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+extern "C" int hclsm_bias_act(const float* x, const float* b, void* y, int64_t rows, int32_t C, int32_t act,
+                              int32_t out_dtype, void* stream) {
+  if (!x || !y) return HCLSM_ERR_NULL;
+  if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
+  if (rows == 0) return HCLSM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (out_dtype == HCLSM_BF16)
+    bias_act_kernel<__nv_bfloat16><<<ew_blocks(rows * C), 256, 0, st>>>(x, b, static_cast<__nv_bfloat16*>(y), rows,
+                                                                        C, act);
+  else if (out_dtype == HCLSM_F32)
+    bias_act_kernel<float><<<ew_blocks(rows * C), 256, 0, st>>>(x, b, static_cast<float*>(y), rows, C, act);
+  else
+    return HCLSM_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+extern "C" int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* out, void* out_bf16,
+                                    int64_t rows, int32_t C, float clamp, void* stream) {
+  if (!h || !m || !out) return HCLSM_ERR_NULL;
+  if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
+  if (rows == 0) return HCLSM_OK;
+  residual_clamp_kernel<<<ew_blocks(rows * C), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      h, m, b, out, static_cast<__nv_bfloat16*>(out_bf16), rows, C, clamp);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}

@@ -1,4 +1,12 @@
 """Mirror of ``hclsm.kernels`` (hclsm/kernels/__init__.py:9-35) backed by sm_100a kernels."""
-from .ssm_scan_kernel import ssm_scan_fn, ssm_scan  # noqa: F401
+from .ssm_scan_kernel import ssm_scan, ssm_scan_fn  # noqa: F401
+from .slot_attention_kernel import (  # noqa: F401
+    SlotIterationParams,
+    slot_attention_core,
+    slot_attention_fn,
+    slot_attention_iteration,
+    slot_attention_iterations,
+)
 
-__all__ = ["ssm_scan_fn", "ssm_scan"]
+__all__ = ["ssm_scan_fn", "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams",
+           "slot_attention_iteration", "slot_attention_iterations"]

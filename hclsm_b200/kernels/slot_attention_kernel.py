@@ -1,0 +1,209 @@
+"""Slot attention on B200 — drop-in for hclsm/kernels/slot_attention_kernel.py
+and for DynamicSlotAttention._iteration_step (hclsm/objects/dynamic_slots.py:98-131).
+
+* ``slot_attention_fn(Q, K, V, scale=None, backend="auto")`` keeps the reference
+  signature (slot_attention_kernel.py:324-355) and returns ``(out, attn)`` with
+  the softmax over the SLOT axis.  The forward runs the fused sm_100a core;
+  the backward applies the reference's own formulas (:215-236) with PyTorch
+  CUDA ops.  ``eps`` (keyword) adds to the softmax denominator: 0 for the
+  naive/compiled reference paths, 1e-8 for its Triton path (:126).
+* ``slot_attention_iteration(slots, k, v, params)`` runs one full refinement
+  step — LayerNorm, W_q, the attention core with the +-30 logit clamp, GRUCell,
+  the residual LayerNorm-MLP and the +-50 clamp — with the attention core and
+  every element-wise stage in this library's kernels and the five weight
+  products as library GEMMs (bf16 operands, fp32 outputs).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _lib
+
+__all__ = ["slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration",
+           "layernorm", "gru_cell", "bias_act", "residual_clamp"]
+
+
+def _c(t):
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def slot_attention_core(Q, K, V, scale=None, *, clamp=0.0, eps=0.0, return_attn=True, attn_fp32=None):
+    """Forward only.  Q (F, N, D), K/V (F, M, D) on CUDA, fp32 or bf16."""
+    _lib.require_cuda(Q, K, V)
+    if Q.dim() != 3 or K.dim() != 3 or V.shape != K.shape or Q.shape[0] != K.shape[0] or Q.shape[2] != K.shape[2]:
+        raise ValueError("expected Q (B, N, D) and K, V (B, M, D)")
+    dt = torch.bfloat16 if {Q.dtype, K.dtype, V.dtype} == {torch.bfloat16} else torch.float32
+    Q, K, V = (_c(t.to(dt)) for t in (Q, K, V))
+    F, N, D = Q.shape
+    M = K.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    out = torch.empty(F, N, D, dtype=dt, device=Q.device)
+    if attn_fp32 is None:
+        attn_fp32 = dt == torch.float32
+    attn = None
+    if return_attn:
+        attn = torch.empty(F, N, M, dtype=torch.float32 if attn_fp32 else dt, device=Q.device)
+    rc = _lib.load().hclsm_slot_attn_core(_lib.ptr(Q), _lib.ptr(K), _lib.ptr(V), _lib.ptr(out), _lib.ptr(attn),
+                                          F, N, M, D, float(scale), float(clamp), float(eps),
+                                          _lib.dtype_code(dt), int(bool(attn_fp32)), _lib.stream_ptr(Q.device))
+    _lib.check(rc, "hclsm_slot_attn_core")
+    return out, attn
+
+
+class _SlotAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, K, V, scale, eps):
+        out, attn = slot_attention_core(Q, K, V, scale, eps=eps, attn_fp32=True)
+        ctx.save_for_backward(Q, K, V, attn)
+        ctx.scale = scale
+        return out.to(Q.dtype), attn if Q.dtype == torch.float32 else attn.to(Q.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_attn):
+        # the reference's backward (slot_attention_kernel.py:215-236)
+        Q, K, V, attn = ctx.saved_tensors
+        f = torch.float32
+        go = grad_out.to(f)
+        d_attn = torch.bmm(go, V.to(f).transpose(1, 2))
+        if grad_attn is not None:
+            d_attn = d_attn + grad_attn.to(f)
+        sum_da = (attn * d_attn).sum(dim=1, keepdim=True)
+        d_logits = attn * (d_attn - sum_da) * ctx.scale
+        dQ = torch.bmm(d_logits, K.to(f)).to(Q.dtype)
+        dK = torch.bmm(d_logits.transpose(1, 2), Q.to(f)).to(K.dtype)
+        dV = torch.bmm(attn.transpose(1, 2), go).to(V.dtype)
+        return dQ, dK, dV, None, None
+
+
+def slot_attention_fn(Q, K, V, scale=None, backend: str = "auto", *, eps: float | None = None):
+    """Drop-in for ``hclsm.kernels.slot_attention_fn``: returns (out, attn) with
+    the softmax over slots.  Every backend name runs the B200 core; ``eps``
+    defaults to the reference backend's value (1e-8 for "triton", else 0)."""
+    if backend not in ("auto", "b200", "triton", "compiled", "naive"):
+        raise ValueError(f"unknown backend {backend!r}")
+    if scale is None:
+        scale = Q.shape[-1] ** -0.5
+    if eps is None:
+        eps = 1e-8 if backend == "triton" else 0.0
+    return _SlotAttn.apply(Q, K, V, float(scale), float(eps))
+
+
+# ---- element-wise stages -------------------------------------------------------------
+def layernorm(x, w=None, b=None, eps=1e-5, out_dtype=torch.float32):
+    x = _c(x.float())
+    rows, D = x.numel() // x.shape[-1], x.shape[-1]
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    rc = _lib.load().hclsm_layernorm(_lib.ptr(x), _lib.ptr(w), _lib.ptr(b), _lib.ptr(y), rows, D, float(eps),
+                                     _lib.dtype_code(out_dtype), _lib.stream_ptr(x.device))
+    _lib.check(rc, "hclsm_layernorm")
+    return y
+
+
+def gru_cell(gi, gh, b_ih, b_hh, h, out=None):
+    H = h.shape[-1]
+    rows = h.numel() // H
+    out = torch.empty_like(h) if out is None else out
+    rc = _lib.load().hclsm_gru_cell(_lib.ptr(gi), _lib.ptr(gh), _lib.ptr(b_ih), _lib.ptr(b_hh), _lib.ptr(h),
+                                    _lib.ptr(out), rows, H, _lib.stream_ptr(h.device))
+    _lib.check(rc, "hclsm_gru_cell")
+    return out
+
+
+def bias_act(x, b, act="relu", out_dtype=torch.bfloat16):
+    C = x.shape[-1]
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    rc = _lib.load().hclsm_bias_act(_lib.ptr(x), _lib.ptr(b), _lib.ptr(y), x.numel() // C, C,
+                                    1 if act == "relu" else 0, _lib.dtype_code(out_dtype), _lib.stream_ptr(x.device))
+    _lib.check(rc, "hclsm_bias_act")
+    return y
+
+
+def residual_clamp(h, m, b, clamp=50.0, out=None, out_bf16=None):
+    C = h.shape[-1]
+    out = torch.empty_like(h) if out is None else out
+    rc = _lib.load().hclsm_residual_clamp(_lib.ptr(h), _lib.ptr(m), _lib.ptr(b), _lib.ptr(out), _lib.ptr(out_bf16),
+                                          h.numel() // C, C, float(clamp), _lib.stream_ptr(h.device))
+    _lib.check(rc, "hclsm_residual_clamp")
+    return out
+
+
+# ---- the fused refinement step -------------------------------------------------------
+@dataclass
+class SlotIterationParams:
+    """Parameters of DynamicSlotAttention used by _iteration_step (names as in
+    hclsm/objects/dynamic_slots.py:44-83), prepared once: weights in bf16
+    (transposed for x @ W^T), biases and LayerNorm affines in fp32."""
+    wq_t: torch.Tensor
+    w_ih_t: torch.Tensor
+    w_hh_t: torch.Tensor
+    b_ih: torch.Tensor
+    b_hh: torch.Tensor
+    w1_t: torch.Tensor
+    b1: torch.Tensor
+    w2_t: torch.Tensor
+    b2: torch.Tensor
+    ln_attn_w: torch.Tensor
+    ln_attn_b: torch.Tensor
+    ln_mlp_w: torch.Tensor
+    ln_mlp_b: torch.Tensor
+    scale: float
+
+    @classmethod
+    def from_state(cls, sd: dict, device, d_slot: int | None = None):
+        def w(name):
+            return sd[name].detach().to(device=device, dtype=torch.bfloat16).t().contiguous()
+
+        def f(name):
+            return sd[name].detach().to(device=device, dtype=torch.float32).contiguous()
+
+        D = d_slot or sd["project_q.weight"].shape[0]
+        return cls(w("project_q.weight"), w("gru.weight_ih"), w("gru.weight_hh"), f("gru.bias_ih"),
+                   f("gru.bias_hh"), w("mlp.0.weight"), f("mlp.0.bias"), w("mlp.2.weight"), f("mlp.2.bias"),
+                   f("norm_pre_attn.weight"), f("norm_pre_attn.bias"), f("norm_slots.weight"),
+                   f("norm_slots.bias"), D ** -0.5)
+
+    @classmethod
+    def from_module(cls, mod):
+        return cls.from_state(dict(mod.named_parameters()), next(mod.parameters()).device, mod.d_slot)
+
+
+def _mm(a, w_t):
+    return torch.mm(a, w_t, out_dtype=torch.float32)
+
+
+def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_bf16=None):
+    """One _iteration_step (dynamic_slots.py:98-131).  slots (F, N, D) fp32 (the
+    carried state), k and v (F, M, D) bf16.  Returns (slots_new fp32, bf16 copy)."""
+    F, N, D = slots.shape
+    R = F * N
+    s2 = slots.reshape(R, D)
+    if slots_bf16 is None:
+        slots_bf16 = s2.to(torch.bfloat16)
+    sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=torch.bfloat16)
+    q = torch.mm(sn, p.wq_t).reshape(F, N, D)
+    upd, _ = slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False)
+    gi = _mm(upd.reshape(R, D), p.w_ih_t)
+    gh = _mm(slots_bf16.reshape(R, D), p.w_hh_t)
+    h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
+    m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=torch.bfloat16)
+    m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
+    m = _mm(m, p.w2_t)
+    out_bf = torch.empty(R, D, dtype=torch.bfloat16, device=slots.device)
+    out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_bf)
+    return out.reshape(F, N, D), out_bf.reshape(F, N, D)
+
+
+def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations: int):
+    s = slots.float().contiguous()
+    sb = None
+    k = _c(k.to(torch.bfloat16))
+    v = _c(v.to(torch.bfloat16))
+    for _ in range(n_iterations):
+        s, sb = slot_attention_iteration(s, k, v, p, sb)
+    return s

@@ -60,3 +60,28 @@ def scan_inputs(nseq, L, d_inner, d_state, dtype=torch.float32, seed=0, device="
     if grad:
         out["dy"] = randn(nseq, L, d_inner).to(dtype)
     return out
+
+
+def slot_inputs(F=128, N=32, M=196, D=384, seed=0, device="cpu"):
+    """Config 2: inputs (F, M, D) = LayerNorm(N(0,1)); initial slots
+    mu + |sigma| * eps with mu, sigma ~ N(0, 0.1) per dim and eps ~ N(0,1);
+    every Linear / GRU weight and bias ~ N(0, 0.02); LayerNorm affines at
+    gamma=1, beta=0.  Parameter names follow DynamicSlotAttention."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape, std=1.0):
+        return torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * std
+
+    inputs = torch.nn.functional.layer_norm(randn(F, M, D), (D,))
+    mu, sigma = randn(D, std=0.1), randn(D, std=0.1)
+    slots = mu + sigma.abs() * randn(F, N, D)
+    w = {}
+    for name, shape in (("project_k.weight", (D, D)), ("project_v.weight", (D, D)), ("project_q.weight", (D, D)),
+                        ("gru.weight_ih", (3 * D, D)), ("gru.weight_hh", (3 * D, D)), ("gru.bias_ih", (3 * D,)),
+                        ("gru.bias_hh", (3 * D,)), ("mlp.0.weight", (4 * D, D)), ("mlp.0.bias", (4 * D,)),
+                        ("mlp.2.weight", (D, 4 * D)), ("mlp.2.bias", (D,))):
+        w[name] = randn(*shape, std=0.02)
+    for name in ("norm_pre_attn", "norm_slots", "norm_input"):
+        w[name + ".weight"] = torch.ones(D, device=device)
+        w[name + ".bias"] = torch.zeros(D, device=device)
+    return {"inputs": inputs, "slots": slots, "weights": w}

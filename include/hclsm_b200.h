@@ -84,6 +84,38 @@ int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const 
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Slot attention core: out = softmax_over_slots(clamp(Q K^T * scale)) V.
+ * Replaces hclsm/kernels/slot_attention_kernel.py:324 slot_attention_fn (the
+ * arithmetic of naive_slot_attention :265-291 with eps=0, of the Triton path
+ * :42-236 with eps=1e-8) and the attention lines of
+ * hclsm/objects/dynamic_slots.py:110-121 (clamp=30).
+ *   Q (F, N, D), K and V (F, M, D), out (F, N, D): dtype (f32 or bf16)
+ *   attn (F, N, M): optional (NULL); f32 when attn_f32, else dtype
+ * clamp <= 0 disables the logit clamp.  bf16: N <= 64, D % 16 == 0, D <= 512,
+ * 16-byte aligned rows; tensor-core MMA with fp32 accumulation.  f32: exact
+ * fp32 arithmetic on CUDA cores.
+ * ------------------------------------------------------------------------- */
+int hclsm_slot_attn_core(const void* Q, const void* K, const void* V, void* out, void* attn, int32_t F,
+                         int32_t N, int32_t M, int32_t D, float scale, float clamp, float eps, int32_t dtype,
+                         int32_t attn_f32, void* stream);
+
+/* Fused element-wise stages of DynamicSlotAttention._iteration_step
+ * (hclsm/objects/dynamic_slots.py:111-130).  Matrices are (rows, C), fp32
+ * unless an out_dtype is given.
+ *   hclsm_layernorm:      y = LayerNorm(x) * w + b   (nn.LayerNorm, :111, :128)
+ *   hclsm_gru_cell:       nn.GRUCell from gi = x W_ih^T, gh = h W_hh^T (:123-126)
+ *   hclsm_bias_act:       y = act(x + b), act 0 = identity, 1 = ReLU (:128 MLP)
+ *   hclsm_residual_clamp: out = clamp(h + m + b, -clamp, clamp), optional bf16 copy (:128-130) */
+int hclsm_layernorm(const float* x, const float* w, const float* b, void* y, int64_t rows, int32_t D, float eps,
+                    int32_t out_dtype, void* stream);
+int hclsm_gru_cell(const float* gi, const float* gh, const float* b_ih, const float* b_hh, const float* h,
+                   float* h_out, int64_t rows, int32_t H, void* stream);
+int hclsm_bias_act(const float* x, const float* b, void* y, int64_t rows, int32_t C, int32_t act,
+                   int32_t out_dtype, void* stream);
+int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* out, void* out_bf16, int64_t rows,
+                         int32_t C, float clamp, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Selective SSM scan, backward, without a caller workspace.
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory when they run the backward (host callbacks, allocator

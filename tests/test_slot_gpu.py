@@ -1,0 +1,90 @@
+"""Parity of the sm_100a slot attention (core and fused iteration) against the
+reference's golden vectors and the CPU oracle.  Tolerances: 1e-5 relative for
+fp32 I/O, 2e-2 relative for bf16 with fp32 accumulation."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import slot_attn as osl
+from hclsm_b200.kernels import (SlotIterationParams, slot_attention_core, slot_attention_fn,
+                                slot_attention_iterations)
+from hclsm_b200.workloads import slot_inputs
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "slot_golden.npz")
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("ci", [0, 1, 2])
+def test_core_golden_fp32(ci):
+    g = np.load(GOLD)
+    Q, K, V = (torch.from_numpy(g[f"core{ci}/{k}"]).cuda() for k in ("Q", "K", "V"))
+    out, attn = slot_attention_fn(Q, K, V, backend="naive")
+    assert rel_err(_np(out), g[f"core{ci}/out"]) < 1e-5
+    assert rel_err(_np(attn), g[f"core{ci}/attn"]) < 1e-5
+    assert torch.allclose(attn.sum(dim=1), torch.ones_like(attn.sum(dim=1)), atol=1e-5)
+
+
+@pytest.mark.parametrize("shape", [(2, 16, 64, 128), (1, 8, 32, 64), (4, 32, 196, 256), (128, 32, 196, 384),
+                                   (3, 5, 33, 64), (2, 64, 130, 512), (1, 17, 1, 16)])
+def test_core_bf16_vs_oracle(shape):
+    B, N, M, D = shape
+    gen = torch.Generator().manual_seed(sum(shape))
+    Q, K, V = (torch.randn(B, n, D, generator=gen).to(torch.bfloat16) for n in (N, M, M))
+    for clamp, eps in ((0.0, 0.0), (30.0, 0.0), (0.0, 1e-8)):
+        out, attn = slot_attention_core(Q.cuda(), K.cuda(), V.cuda(), clamp=clamp, eps=eps, attn_fp32=True)
+        Qn, Kn, Vn = (t.float().numpy() for t in (Q, K, V))
+        logits = (Qn @ Kn.transpose(0, 2, 1)) * D ** -0.5
+        if clamp:
+            logits = np.clip(logits, -clamp, clamp)
+        e = np.exp(logits - logits.max(1, keepdims=True))
+        a = e / (e.sum(1, keepdims=True) + eps)
+        assert rel_err(_np(attn), a) < 2e-2
+        assert rel_err(_np(out), a @ Vn) < 2e-2
+
+
+def test_core_backward_matches_autograd():
+    gen = torch.Generator().manual_seed(3)
+    Q, K, V = (torch.randn(2, n, 64, generator=gen).cuda().requires_grad_(True) for n in (8, 40, 40))
+    out, attn = slot_attention_fn(Q, K, V)
+    (out.square().sum() + attn.sum()).backward()
+    Q2, K2, V2 = (t.detach().clone().requires_grad_(True) for t in (Q, K, V))
+    lg = torch.bmm(Q2, K2.transpose(1, 2)) * 64 ** -0.5
+    a = torch.softmax(lg, dim=1)
+    o = torch.bmm(a, V2)
+    (o.square().sum() + a.sum()).backward()
+    for x, y in ((Q, Q2), (K, K2), (V, V2)):
+        assert rel_err(_np(x.grad), _np(y.grad)) < 1e-4
+
+
+def test_iterations_golden():
+    g = np.load(GOLD)
+    W = {k[len("iter/w/"):]: torch.from_numpy(g[k]) for k in g.files if k.startswith("iter/w/")}
+    p = SlotIterationParams.from_state(W, "cuda")
+    k, v = (torch.from_numpy(g[f"iter/{n}"]).cuda() for n in ("k", "v"))
+    s = torch.from_numpy(g["iter/slots0"]).cuda()
+    out = slot_attention_iterations(s, k, v, p, 3)
+    assert rel_err(_np(out), g["iter/slots3"]) < 2e-2
+
+
+def test_config2_three_iterations_vs_oracle():
+    d = slot_inputs(seed=0)
+    W = d["weights"]
+    Wq = {k: t.to(torch.bfloat16).float() if t.dim() == 2 else t for k, t in W.items()}
+    # k and v as DynamicSlotAttention.forward builds them (dynamic_slots.py:152-154)
+    inp = d["inputs"].to(torch.bfloat16).float()
+    k = (inp @ Wq["project_k.weight"].T).to(torch.bfloat16)
+    v = (inp @ Wq["project_v.weight"].T).to(torch.bfloat16)
+    p = SlotIterationParams.from_state(W, "cuda")
+    out = slot_attention_iterations(d["slots"].cuda(), k.cuda(), v.cuda(), p, 3)
+    Wn = {kk: t.numpy() for kk, t in Wq.items()}
+    s = d["slots"].numpy()
+    for _ in range(3):
+        s = osl.iteration_step(s, k.float().numpy(), v.float().numpy(), Wn)
+    assert rel_err(_np(out), s) < 2e-2
