@@ -8,5 +8,11 @@ from .slot_attention_kernel import (  # noqa: F401
     slot_attention_iterations,
 )
 
-__all__ = ["ssm_scan_fn", "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams",
+from .sparse_event_attn import (  # noqa: F401
+    EventTransformer,
+    sparse_event_attention_fused,
+    sparse_event_attn_fn,
+)
+
+__all__ = ["sparse_event_attn_fn", "EventTransformer", "sparse_event_attention_fused", "ssm_scan_fn", "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams",
            "slot_attention_iteration", "slot_attention_iterations"]

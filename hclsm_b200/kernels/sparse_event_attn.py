@@ -1,0 +1,215 @@
+"""Sparse event attention on B200 — drop-in for hclsm/kernels/sparse_event_attn.py.
+
+* ``sparse_event_attn_fn(states, event_mask, attn_fn, max_events=None, backend="auto")``
+  keeps the reference signature (sparse_event_attn.py:242-263).  Fired frames
+  are found by a device-side stream compaction (video-major, ascending time,
+  as the reference's ``nonzero`` loop :62-67), gathered, passed to ``attn_fn``
+  and merged back by one fused copy+scatter kernel.  A Python ``attn_fn``
+  receives the reference's padded (B * K_max, N, D) batch with zero pad frames
+  (:58-78); an ``EventTransformer`` (Level1EventDynamics weights) runs the
+  fused transformer on the compacted frames only.
+* ``EventTransformer`` restates Level1EventDynamics.forward
+  (hclsm/dynamics/level1_event.py:85-133) with this library's kernels: per layer
+  LayerNorm -> qkv GEMM -> per-frame multi-head attention (tensor cores) ->
+  out-proj GEMM + residual; LayerNorm -> [W1 | W3] GEMM -> SwiGLU -> W2 GEMM +
+  residual; final LayerNorm and proj_out.  GEMMs are library GEMMs with bf16
+  operands and fp32 outputs for bf16 inputs, fp32 throughout for fp32 inputs.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import _lib
+from .slot_attention_kernel import layernorm, residual_clamp
+
+__all__ = ["sparse_event_attn_fn", "EventTransformer", "event_compact", "event_gather", "event_scatter",
+           "sparse_event_attention_fused"]
+
+
+def _c(t):
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+# ---- compaction / gather / scatter ---------------------------------------------------
+def event_compact(event_mask):
+    """Device-side compaction of a (B, T) mask.  Returns (idx, pos, counts, meta)
+    int32 tensors: idx[k] = b*T + t of the k-th fired frame, pos[b*T+t] = k or
+    -1, counts[b] per video, meta = [total, max per video]."""
+    m = event_mask
+    if m.dtype not in (torch.float32, torch.bfloat16):
+        m = m.float()
+    m = _c(m)
+    B, T = m.shape
+    dev = m.device
+    idx = torch.empty(max(B * T, 1), dtype=torch.int32, device=dev)
+    pos = torch.empty(max(B * T, 1), dtype=torch.int32, device=dev)
+    counts = torch.empty(max(B, 1), dtype=torch.int32, device=dev)
+    meta = torch.empty(2, dtype=torch.int32, device=dev)
+    rc = _lib.load().hclsm_event_compact(_lib.ptr(m), _lib.dtype_code(m.dtype), B, T, _lib.ptr(idx), _lib.ptr(pos),
+                                         _lib.ptr(counts), _lib.ptr(meta), _lib.stream_ptr(dev))
+    _lib.check(rc, "hclsm_event_compact")
+    return idx, pos, counts, meta
+
+
+def event_gather(states, idx, counts, meta, n_frames, pad_k=0):
+    """(n_frames, N, D) compacted frames (pad_k=0) or the padded (B*pad_k, N, D)
+    layout with zero pad frames."""
+    B, T, N, D = states.shape
+    out = torch.empty(n_frames, N, D, dtype=states.dtype, device=states.device)
+    if n_frames == 0:
+        return out
+    rc = _lib.load().hclsm_event_gather(_lib.ptr(states), _lib.ptr(idx), _lib.ptr(counts), _lib.ptr(meta),
+                                        _lib.ptr(out), N * D, B, pad_k, n_frames, _lib.dtype_code(states.dtype),
+                                        _lib.stream_ptr(states.device))
+    _lib.check(rc, "hclsm_event_gather")
+    return out
+
+
+def event_scatter(states, upd, pos, counts, pad_k=0):
+    """A copy of states with every fired frame replaced by its update."""
+    B, T, N, D = states.shape
+    out = torch.empty_like(states)
+    upd = upd if upd.numel() else states  # no events: plain copy
+    rc = _lib.load().hclsm_event_scatter(_lib.ptr(states), _lib.ptr(_c(upd)), _lib.ptr(pos), _lib.ptr(counts),
+                                         _lib.ptr(out), B * T, N * D, T, pad_k, _lib.dtype_code(states.dtype),
+                                         _lib.stream_ptr(states.device))
+    _lib.check(rc, "hclsm_event_scatter")
+    return out
+
+
+# ---- Level-1 event transformer -----------------------------------------------------------
+@dataclass
+class _Layer:
+    ln1_w: torch.Tensor
+    ln1_b: torch.Tensor
+    w_qkv_t: torch.Tensor
+    w_o_t: torch.Tensor
+    ln2_w: torch.Tensor
+    ln2_b: torch.Tensor
+    w13_t: torch.Tensor
+    w2_t: torch.Tensor
+
+
+@dataclass
+class EventTransformer:
+    """Weights of Level1EventDynamics prepared for the fused path (parameter
+    names of hclsm/dynamics/level1_event.py).  Callable on (frames, N, d_slot)."""
+    n_heads: int
+    w_in_t: torch.Tensor
+    w_out_t: torch.Tensor
+    norm_w: torch.Tensor
+    norm_b: torch.Tensor
+    layers: list = field(default_factory=list)
+    dtype: torch.dtype = torch.bfloat16
+
+    @classmethod
+    def from_state(cls, sd: dict, n_heads: int, device, dtype=torch.bfloat16):
+        def w(name):
+            return sd[name].detach().to(device=device, dtype=dtype).t().contiguous()
+
+        def f(name):
+            return sd[name].detach().to(device=device, dtype=torch.float32).contiguous()
+
+        n_layers = 1 + max(int(k.split(".")[1]) for k in sd if k.startswith("blocks."))
+        layers = []
+        for i in range(n_layers):
+            p = f"blocks.{i}."
+            w13 = torch.cat([sd[p + "ffn.w1.weight"], sd[p + "ffn.w3.weight"]], 0)
+            layers.append(_Layer(f(p + "norm1.weight"), f(p + "norm1.bias"), w(p + "attn.in_proj_weight"),
+                                 w(p + "attn.out_proj.weight"), f(p + "norm2.weight"), f(p + "norm2.bias"),
+                                 w13.detach().to(device=device, dtype=dtype).t().contiguous(),
+                                 w(p + "ffn.w2.weight")))
+        return cls(n_heads, w("proj_in.weight"), w("proj_out.weight"), f("norm.weight"), f("norm.bias"), layers,
+                   dtype)
+
+    @classmethod
+    def from_module(cls, mod, dtype=torch.bfloat16):
+        heads = mod.blocks[0].attn.num_heads
+        return cls.from_state(dict(mod.named_parameters()), heads, next(mod.parameters()).device, dtype)
+
+    def _mm(self, a, w_t):
+        if self.dtype == torch.float32:
+            return torch.mm(a, w_t)
+        return torch.mm(a, w_t, out_dtype=torch.float32)
+
+    def __call__(self, frames, key_padding_mask=None):
+        """frames (n, N, d_slot) -> (n, N, d_slot); key_padding_mask (n, N) bool,
+        True = dead slot (ignored as a key)."""
+        n, N, Ds = frames.shape
+        if n == 0:
+            return frames.clone()
+        dt = self.dtype
+        E = self.w_in_t.shape[1]
+        H = self.n_heads
+        hd = E // H
+        R = n * N
+        x = self._mm(_c(frames.to(dt)).reshape(R, Ds), self.w_in_t)  # fp32 residual stream
+        kp = None
+        if key_padding_mask is not None:
+            kp = _c(key_padding_mask.to(torch.uint8))
+        lib = _lib.load()
+        for ly in self.layers:
+            h = layernorm(x, ly.ln1_w, ly.ln1_b, out_dtype=dt)
+            qkv = _c(torch.mm(h, ly.w_qkv_t))
+            a = torch.empty(R, E, dtype=dt, device=x.device)
+            rc = lib.hclsm_event_mha(_lib.ptr(qkv), _lib.ptr(kp), _lib.ptr(a), n, N, H, hd, float(hd ** -0.5),
+                                     _lib.dtype_code(dt), _lib.stream_ptr(x.device))
+            _lib.check(rc, "hclsm_event_mha")
+            x = residual_clamp(x, self._mm(a, ly.w_o_t), None, 0.0)
+            h = layernorm(x, ly.ln2_w, ly.ln2_b, out_dtype=dt)
+            u = self._mm(h, ly.w13_t)
+            F = u.shape[1] // 2
+            s = torch.empty(R, F, dtype=dt, device=x.device)
+            rc = lib.hclsm_swiglu(_lib.ptr(u), _lib.ptr(s), R, F, _lib.dtype_code(dt), _lib.stream_ptr(x.device))
+            _lib.check(rc, "hclsm_swiglu")
+            x = residual_clamp(x, self._mm(s, ly.w2_t), None, 0.0)
+        h = layernorm(x, self.norm_w, self.norm_b, out_dtype=dt)
+        y = self._mm(h, self.w_out_t)
+        return y.reshape(n, N, -1).to(frames.dtype)
+
+
+def sparse_event_attention_fused(states, event_mask, transformer: EventTransformer, obj_mask=None):
+    """Events of ``states`` (B, T, N, D) updated by the Level-1 transformer;
+    obj_mask (B, N) (alive > 0.5) masks dead slots as keys, as the model does
+    (level1_event.py:108-112)."""
+    _lib.require_cuda(states, event_mask)
+    states = _c(states)
+    B, T, N, D = states.shape
+    idx, pos, counts, meta = event_compact(event_mask)
+    n = int(meta[0].item())  # one host read (the reference syncs for K_max too)
+    frames = event_gather(states, idx, counts, meta, n)
+    kp = None
+    if obj_mask is not None:
+        dead = ~(obj_mask > 0.5)
+        kp = dead[(idx[:n].long() // T)]
+    upd = transformer(frames, kp)
+    return event_scatter(states, upd.to(states.dtype), pos, counts)
+
+
+def sparse_event_attn_fn(states, event_mask, attn_fn, max_events=None, backend: str = "auto"):
+    """Drop-in for ``hclsm.kernels.sparse_event_attn_fn``.  ``attn_fn`` maps
+    (B*K, N, D) -> (B*K, N, D); an ``EventTransformer`` takes the fused path."""
+    if backend not in ("auto", "b200", "optimized", "naive"):
+        raise ValueError(f"unknown backend {backend!r}")
+    _lib.require_cuda(states, event_mask)
+    if isinstance(attn_fn, EventTransformer) and max_events is None:
+        return sparse_event_attention_fused(states, event_mask, attn_fn)
+    states = _c(states)
+    B, T, N, D = states.shape
+    idx, pos, counts, meta = event_compact(event_mask)
+    kmax = int(meta[1].item())
+    K = max(kmax if max_events is None else max_events, 1)
+    if max_events is not None and max_events < kmax:
+        # truncation: keep the first max_events events of each video (:64-67)
+        m = (event_mask > 0.5)
+        rank = torch.cumsum(m.int(), dim=1) - 1
+        m = m & (rank < max_events)
+        idx, pos, counts, meta = event_compact(m.float())
+    padded = event_gather(states, idx, counts, meta, B * K, pad_k=K)
+    upd = attn_fn(padded.reshape(B * K, N, D))
+    return event_scatter(states, upd.reshape(B * K, N, D).to(states.dtype), pos, counts, pad_k=K)

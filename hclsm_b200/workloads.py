@@ -85,3 +85,33 @@ def slot_inputs(F=128, N=32, M=196, D=384, seed=0, device="cpu"):
         w[name + ".weight"] = torch.ones(D, device=device)
         w[name + ".bias"] = torch.zeros(D, device=device)
     return {"inputs": inputs, "slots": slots, "weights": w}
+
+
+def event_inputs(B=8, T=64, N=32, D=384, heads=6, layers=3, p=0.1, seed=0, device="cpu"):
+    """Config 3: states (B, T, N, D) ~ N(0,1); event mask ~ Bernoulli(p) per
+    (video, t), with t=0 forced on for a video without events (as
+    event_detector.py:167-170 guarantees one event); Level1EventDynamics
+    weights ~ N(0, 0.02) (d_model = D, SwiGLU hidden 4D), LayerNorm affines at
+    gamma=1, beta=0.  Parameter names follow Level1EventDynamics."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape, std=1.0):
+        return torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * std
+
+    states = randn(B, T, N, D)
+    mask = (torch.rand(B, T, generator=g, device=device) < p).float()
+    none = mask.sum(1) == 0
+    mask[none, 0] = 1.0
+    w = {"proj_in.weight": randn(D, D, std=0.02), "proj_out.weight": randn(D, D, std=0.02),
+         "norm.weight": torch.ones(D, device=device), "norm.bias": torch.zeros(D, device=device)}
+    for i in range(layers):
+        q = f"blocks.{i}."
+        w[q + "attn.in_proj_weight"] = randn(3 * D, D, std=0.02)
+        w[q + "attn.out_proj.weight"] = randn(D, D, std=0.02)
+        w[q + "ffn.w1.weight"] = randn(4 * D, D, std=0.02)
+        w[q + "ffn.w3.weight"] = randn(4 * D, D, std=0.02)
+        w[q + "ffn.w2.weight"] = randn(D, 4 * D, std=0.02)
+        for nm in ("norm1", "norm2"):
+            w[q + nm + ".weight"] = torch.ones(D, device=device)
+            w[q + nm + ".bias"] = torch.zeros(D, device=device)
+    return {"states": states, "mask": mask, "weights": w, "heads": heads, "layers": layers}

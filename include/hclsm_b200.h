@@ -116,6 +116,39 @@ int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* 
                          int32_t C, float clamp, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Sparse event attention.  Replaces the gather / scatter of
+ * hclsm/kernels/sparse_event_attn.py:35-188 and
+ * hclsm/dynamics/hierarchy_manager.py:42-118, and the attention and SwiGLU of
+ * hclsm/dynamics/level1_event.py:17-54.
+ *   hclsm_event_compact: (B, T) mask (f32/bf16, fired > 0.5) -> idx[k] =
+ *       b*T + t of the k-th fired frame (video-major, time ascending),
+ *       pos[b*T + t] = k or -1, counts[b], meta = {total, max per video}.
+ *       Runs on the device; nothing is read back.
+ *   hclsm_event_gather: frames (frame_elems elements each) of the fired
+ *       timesteps: compact (pad_k = 0, rows >= meta[0] untouched) or padded
+ *       (B, pad_k) with zero pad frames.
+ *   hclsm_event_scatter: out = states with every fired frame replaced by its
+ *       update (the reference's clone + scatter in one pass).
+ *   hclsm_event_mha: per-frame multi-head self-attention of
+ *       nn.MultiheadAttention(bias=False) on a packed (frames*T, 3E) q|k|v
+ *       matrix; key_pad (frames, T) bytes, non-zero = ignored key (NULL: none).
+ *       bf16: T <= 64, head dim in {16, 32, 64, 128}, tensor cores.
+ *   hclsm_swiglu: y = silu(u[:, :C]) * u[:, C:] (SwiGLUFFN, level1_event.py:28).
+ * frame_elems * element size must be a multiple of 16 bytes.
+ * ------------------------------------------------------------------------- */
+int hclsm_event_compact(const void* mask, int32_t mask_dtype, int32_t B, int32_t T, int32_t* idx, int32_t* pos,
+                        int32_t* counts, int32_t* meta, void* stream);
+int hclsm_event_gather(const void* states, const int32_t* idx, const int32_t* counts, const int32_t* meta,
+                       void* out, int64_t frame_elems, int32_t B, int32_t pad_k, int64_t max_frames,
+                       int32_t dtype, void* stream);
+int hclsm_event_scatter(const void* states, const void* upd, const int32_t* pos, const int32_t* counts, void* out,
+                        int64_t frames, int64_t frame_elems, int32_t T, int32_t pad_k, int32_t dtype,
+                        void* stream);
+int hclsm_event_mha(const void* qkv, const uint8_t* key_pad, void* out, int32_t frames, int32_t T, int32_t H,
+                    int32_t HD, float scale, int32_t dtype, void* stream);
+int hclsm_swiglu(const float* u, void* y, int64_t rows, int32_t C, int32_t out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Selective SSM scan, backward, without a caller workspace.
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory when they run the backward (host callbacks, allocator

@@ -1,0 +1,103 @@
+"""Parity of the sm_100a sparse event attention against the reference's golden
+vectors, its known-answer tests and the CPU oracle (1e-5 relative for fp32,
+2e-2 relative for bf16)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import event_attn as oev
+from hclsm_b200.kernels import EventTransformer, sparse_event_attention_fused, sparse_event_attn_fn
+from hclsm_b200.kernels.sparse_event_attn import event_compact
+from hclsm_b200.workloads import event_inputs
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "event_golden.npz")
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _gold():
+    g = np.load(GOLD)
+    W = {k[len("ev/w/"):]: torch.from_numpy(g[k]) for k in g.files if k.startswith("ev/w/")}
+    return g, W
+
+
+def test_golden_fp32_fused_and_callable():
+    g, W = _gold()
+    tr = EventTransformer.from_state(W, int(g["ev/n_heads"]), "cuda", dtype=torch.float32)
+    st, m = torch.from_numpy(g["ev/states"]).cuda(), torch.from_numpy(g["ev/mask"]).cuda()
+    assert rel_err(_np(sparse_event_attn_fn(st, m, tr)), g["ev/y_naive"]) < 1e-5
+    # a Python attn_fn sees the reference's padded batch
+    assert rel_err(_np(sparse_event_attn_fn(st, m, lambda f: tr(f))), g["ev/y_vectorized"]) < 1e-5
+
+
+def test_golden_model_path_with_dead_slots():
+    g, W = _gold()
+    tr = EventTransformer.from_state(W, int(g["ev/n_heads"]), "cuda", dtype=torch.float32)
+    st, m = torch.from_numpy(g["ev/states"]).cuda(), torch.from_numpy(g["ev/mask"]).cuda()
+    alive = torch.from_numpy(g["ev/alive"]).cuda()
+    y = sparse_event_attention_fused(st, m, tr, obj_mask=alive)
+    assert rel_err(_np(y), g["ev/y_model"]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_known_answers(dtype):
+    """tests/test_kernels.py:182-232 of the reference."""
+    st = torch.randn(2, 16, 8, 32).to(dtype).cuda()
+    m = torch.zeros(2, 16, device="cuda")
+    m[0, [2, 5, 10]] = 1
+    m[1, [1, 7]] = 1
+    out = sparse_event_attn_fn(st, m, lambda x: x * 2.0)
+    assert torch.equal(out[0, 0], st[0, 0]) and torch.equal(out[0, 3], st[0, 3])
+    assert torch.equal(out[0, 2], st[0, 2] * 2) and torch.equal(out[1, 7], st[1, 7] * 2)
+    assert torch.equal(sparse_event_attn_fn(st, torch.zeros(2, 16, device="cuda"), lambda x: x), st)
+    assert torch.all(sparse_event_attn_fn(st, torch.ones(2, 16, device="cuda"), lambda x: x * 0) == 0)
+    m2 = torch.zeros(2, 16, device="cuda")
+    m2[0, [2, 5, 10]] = 1
+    m2[1, [1, 7, 9, 14]] = 1
+    ident = sparse_event_attn_fn(st, m2, lambda x: x)
+    assert torch.equal(ident, st)
+
+
+def test_compaction_matches_nonzero_order():
+    gen = torch.Generator().manual_seed(5)
+    m = (torch.rand(7, 300, generator=gen) < 0.3).float()
+    idx, pos, counts, meta = event_compact(m.cuda())
+    nz = torch.nonzero(m.reshape(-1) > 0.5).flatten()
+    n = int(meta[0])
+    assert n == len(nz) and torch.equal(idx[:n].cpu().long(), nz)
+    assert torch.equal(counts[:7].cpu(), (m > 0.5).sum(1).int())
+    assert int(meta[1]) == int((m > 0.5).sum(1).max())
+    p = pos.cpu()
+    assert torch.equal(p[nz], torch.arange(n, dtype=torch.int32))
+
+
+def test_max_events_truncates():
+    st = torch.randn(2, 10, 4, 16).cuda()
+    m = torch.zeros(2, 10, device="cuda")
+    m[0, [1, 3, 6]] = 1
+    m[1, [0, 9]] = 1
+    out = sparse_event_attn_fn(st, m, lambda x: x + 1.0, max_events=2)
+    ref = oev.naive_sparse_event_attention(_np(st), _np(m), lambda f: f + 1.0, max_events=2)
+    assert np.array_equal(_np(out), ref)
+
+
+def test_config3_bf16_vs_oracle():
+    d = event_inputs(seed=0)
+    W = d["weights"]
+    Wq = {k: (t.to(torch.bfloat16).float() if t.dim() == 2 else t) for k, t in W.items()}
+    tr = EventTransformer.from_state(W, d["heads"], "cuda", dtype=torch.bfloat16)
+    st = d["states"].to(torch.bfloat16)
+    y = sparse_event_attn_fn(st.cuda(), d["mask"].cuda(), tr)
+    Wn = {k: t.numpy() for k, t in Wq.items()}
+    ref = oev.naive_sparse_event_attention(st.float().numpy(), d["mask"].numpy(),
+                                           lambda f: oev.level1_event(f, Wn, d["heads"], d["layers"]))
+    assert rel_err(_np(y), ref) < 2e-2
+    # non-event frames are bit-identical copies
+    nz = d["mask"] < 0.5
+    assert torch.equal(y.cpu()[nz], st[nz])
