@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--ref-seqs", type=int, default=16, help="sequences per CPU-baseline step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the slot / event attention legs")
     return ap.parse_args()
 
 
@@ -242,6 +243,98 @@ def run_e2e(args, rank, world, dev):
             "d2h_bytes_per_step": d2h, "ms_per_step": ms, "sequences_per_rank": n}
 
 
+SLOT_FLOP_PER_FRAME = 7.29e10 / 128  # config 2: QK^T, attn V, W_q, GRU, MLP over 3 iterations + k/v proj
+
+
+def run_slot(args, rank, world, dev):
+    """Config 2: DynamicSlotAttention k/v projections + 3 fused iterations on 128
+    frames (32 slots, 196 tokens, dim 384, bf16), captured in a CUDA graph."""
+    import torch
+    import torch.distributed as dist
+
+    from hclsm_b200.kernels import SlotIterationParams, slot_attention_iterations
+    from hclsm_b200.workloads import slot_inputs
+
+    d = slot_inputs(seed=10 + rank, device=dev)
+    W = d["weights"]
+    p = SlotIterationParams.from_state(W, dev)
+    wk = W["project_k.weight"].to(torch.bfloat16).t().contiguous()
+    wv = W["project_v.weight"].to(torch.bfloat16).t().contiguous()
+    inp = d["inputs"].to(torch.bfloat16)
+    F_, M, D = inp.shape
+
+    def step():
+        x = inp.reshape(F_ * M, D)
+        k = torch.mm(x, wk).reshape(F_, M, D)
+        v = torch.mm(x, wv).reshape(F_, M, D)
+        return slot_attention_iterations(d["slots"], k, v, p, 3)
+
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(args.warmup):
+        g.replay()
+    reps = 20
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    return {"metric": "slot_attention_frames_per_s", "value": F_ * world / (ms * 1e-3), "unit": "frames/s",
+            "ms_per_step": ms, "config": "BASELINE config 2: 128 frames x 32 slots x 196 tokens x 384, 3 iterations, "
+                                         "bf16, k/v projections included, CUDA graph",
+            "tflops": SLOT_FLOP_PER_FRAME * F_ / (ms * 1e-3) / 1e12}
+
+
+def run_event(args, rank, world, dev):
+    """Config 3: sparse event attention with the 3-layer Level-1 transformer over
+    8 videos x 64 steps x 32 slots x 384 (bf16), Bernoulli(0.1) event mask."""
+    import torch
+    import torch.distributed as dist
+
+    from hclsm_b200.kernels import EventTransformer, sparse_event_attn_fn
+    from hclsm_b200.workloads import event_inputs
+
+    d = event_inputs(seed=20 + rank, device=dev)
+    tr = EventTransformer.from_state(d["weights"], d["heads"], dev, dtype=torch.bfloat16)
+    st = d["states"].to(torch.bfloat16)
+    m = d["mask"]
+    for _ in range(args.warmup):
+        sparse_event_attn_fn(st, m, tr)
+    reps = 20
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        sparse_event_attn_fn(st, m, tr)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    n_ev = int(m.sum().item())
+    return {"metric": "sparse_event_attention_events_per_s", "value": n_ev * world / (ms * 1e-3),
+            "unit": "event frames/s", "ms_per_call": ms, "event_frames": n_ev,
+            "config": "BASELINE config 3: 8 videos x 64 steps x 32 slots x 384, 6 heads, 3 layers, p=0.1, bf16"}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -276,6 +369,9 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     r = run_b200(args, rank, world, local_rank)
+    dev = torch.device("cuda", local_rank)
+    slot = None if args.no_extra else run_slot(args, rank, world, dev)
+    event = None if args.no_extra else run_event(args, rank, world, dev)
     cpu = None
     if rank == 0 and not args.no_cpu:
         v, cores, _ = cpu_reference(args.ref_seqs, 1, 1)
@@ -309,6 +405,7 @@ def main():
                 "roofline_fwd": {"kernel": "scan_fwd (hclsm_ssm_scan_fwd)", "achieved": bw_fwd,
                                  "frac": bw_fwd / hbm_peak, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes},
                 "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
+                "slot_attention": slot, "event_attention": event,
                 "gpu_launches": 5 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:

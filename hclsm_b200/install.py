@@ -1,0 +1,194 @@
+"""Patch a loaded ``hclsm`` package so its own call sites run the B200 kernels.
+
+    import hclsm, hclsm_b200
+    hclsm_b200.install()          # or install(hclsm) for an explicit module
+
+What is replaced (paths inside RightNow-AI/hclsm):
+
+* ``hclsm.kernels.ssm_scan_fn`` and ``hclsm.kernels.ssm_scan_kernel.ssm_scan_fn``
+  (the package re-exports by value, hclsm/kernels/__init__.py:9-35, so both
+  names are patched), likewise ``slot_attention_fn`` and ``sparse_event_attn_fn``;
+* ``SimplifiedSSMBlock.forward`` (hclsm/dynamics/level0_ssm.py:58-107): the
+  inline clamped scan and the SiLU gate run as one differentiable kernel call
+  (clamp=True, z = gate_proj(x));
+* ``DynamicSlotAttention._iteration_step`` (hclsm/objects/dynamic_slots.py:98-131);
+* ``HierarchyManager.gather_events`` / ``scatter_events``
+  (hclsm/dynamics/hierarchy_manager.py:42-118);
+* ``Level1EventDynamics.forward`` (hclsm/dynamics/level1_event.py:85-133).
+
+The scan is differentiable.  The slot-attention step, the event gather /
+scatter and the Level-1 transformer are forward kernels: they replace the
+reference while autograd is off (inference, planning, evaluation) and defer to
+the reference's own implementation while a gradient is being recorded.  CPU
+tensors are not accepted by the replaced functions (no CPU fallback).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+_ORIG = {}
+
+
+def _grad_active(*tensors):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def _patch(obj, name, new):
+    key = (id(obj), name)
+    if key not in _ORIG:
+        _ORIG[key] = (obj, name, getattr(obj, name))
+    setattr(obj, name, new)
+
+
+def _orig(obj, name):
+    """The attribute as it was before install() (so a second install() does not wrap twice)."""
+    ent = _ORIG.get((id(obj), name))
+    return ent[2] if ent else getattr(obj, name)
+
+
+def uninstall():
+    """Restore every attribute install() replaced."""
+    for obj, name, old in list(_ORIG.values()):
+        setattr(obj, name, old)
+    _ORIG.clear()
+
+
+def _ssm_block_forward(self, x):
+    """SimplifiedSSMBlock.forward with the scan and gate fused (level0_ssm.py:58-107)."""
+    from .kernels import ssm_scan
+
+    residual = x
+    x = self.norm(x)
+    z = self.in_proj(x)
+    gate_pre = self.gate_proj(x)
+    dt = F.softplus(self.dt_proj(z)).clamp(min=1e-3, max=1.0)
+    B_param = self.B_proj(z)
+    C_param = self.C_proj(z)
+    y = ssm_scan(z, dt, self.A_log, B_param, C_param, clamp=True, z=gate_pre)
+    y = self.out_proj(y.to(residual.dtype))
+    return residual + y
+
+
+def _make_iteration_step(orig):
+    def _iteration_step(self, slots, k, v):
+        if _grad_active(slots, k, v) or any(p.requires_grad for p in self.parameters()) and torch.is_grad_enabled():
+            return orig(self, slots, k, v)
+        from .kernels.slot_attention_kernel import SlotIterationParams, slot_attention_iteration
+
+        key = tuple(p._version for p in self.parameters())
+        cache = getattr(self, "_hclsm_b200_params", None)
+        if cache is None or cache[0] != key:
+            cache = (key, SlotIterationParams.from_module(self))
+            self._hclsm_b200_params = cache
+        kb = k.to(torch.bfloat16).contiguous()
+        vb = v.to(torch.bfloat16).contiguous()
+        out, _ = slot_attention_iteration(slots.float().contiguous(), kb, vb, cache[1])
+        return out.to(slots.dtype)
+
+    return _iteration_step
+
+
+def _make_gather(orig):
+    def gather_events(self, states, event_mask):
+        if _grad_active(states):
+            return orig(self, states, event_mask)
+        from .kernels.sparse_event_attn import event_compact, event_gather
+
+        B, T, N, D = states.shape
+        st = states.contiguous()
+        idx, pos, counts, meta = event_compact(event_mask)
+        kmax = max(int(meta[1].item()), 1)
+        ev = event_gather(st, idx, counts, meta, B * kmax, pad_k=kmax).reshape(B, kmax, N, D)
+        pad = (torch.arange(kmax, device=states.device)[None, :] < counts[:B, None]).float()
+        return ev, pad, kmax
+
+    return gather_events
+
+
+def _make_scatter(orig):
+    def scatter_events(self, base_states, event_updates, event_mask):
+        if _grad_active(base_states, event_updates):
+            return orig(self, base_states, event_updates, event_mask)
+        from .kernels.sparse_event_attn import event_compact, event_scatter
+
+        K = event_updates.shape[1]
+        m = (event_mask > 0.5)
+        rank = torch.cumsum(m.int(), dim=1) - 1
+        idx, pos, counts, meta = event_compact((m & (rank < K)).float())
+        upd = event_updates.reshape(-1, *event_updates.shape[2:]).to(base_states.dtype).contiguous()
+        return event_scatter(base_states.contiguous(), upd, pos, counts, pad_k=K)
+
+    return scatter_events
+
+
+def _make_level1_forward(orig):
+    def forward(self, event_states, event_pad_mask=None, obj_mask=None):
+        if _grad_active(event_states) or any(p.requires_grad for p in self.parameters()) and torch.is_grad_enabled():
+            return orig(self, event_states, event_pad_mask, obj_mask)
+        from .kernels.sparse_event_attn import EventTransformer
+
+        key = tuple(p._version for p in self.parameters())
+        cache = getattr(self, "_hclsm_b200_tr", None)
+        dtype = torch.bfloat16 if event_states.dtype == torch.bfloat16 else torch.float32
+        if cache is None or cache[0] != (key, dtype):
+            cache = ((key, dtype), EventTransformer.from_module(self, dtype))
+            self._hclsm_b200_tr = cache
+        B, K, N, D = event_states.shape
+        kp = None
+        if obj_mask is not None:
+            kp = (~(obj_mask > 0.5)).unsqueeze(1).expand(B, K, N).reshape(B * K, N)
+        y = cache[1](event_states.reshape(B * K, N, D), kp).reshape(B, K, N, -1)
+        if event_pad_mask is not None:
+            y = y * event_pad_mask[:, :, None, None]
+        return y
+
+    return forward
+
+
+def install(hclsm_module=None):
+    """Patch ``hclsm`` (imported if not given).  Returns the list of patched names."""
+    if hclsm_module is None:
+        import importlib
+
+        hclsm_module = importlib.import_module("hclsm")
+    from . import kernels as k
+
+    done = []
+    kern = getattr(hclsm_module, "kernels", None)
+    if kern is not None:
+        for name, fn in (("ssm_scan_fn", k.ssm_scan_fn), ("slot_attention_fn", k.slot_attention_fn),
+                         ("sparse_event_attn_fn", k.sparse_event_attn_fn)):
+            if hasattr(kern, name):
+                _patch(kern, name, fn)
+                done.append(f"kernels.{name}")
+        for sub, name, fn in (("ssm_scan_kernel", "ssm_scan_fn", k.ssm_scan_fn),
+                              ("slot_attention_kernel", "slot_attention_fn", k.slot_attention_fn),
+                              ("sparse_event_attn", "sparse_event_attn_fn", k.sparse_event_attn_fn)):
+            mod = getattr(kern, sub, None)
+            if mod is not None and hasattr(mod, name):
+                _patch(mod, name, fn)
+                done.append(f"kernels.{sub}.{name}")
+    dyn = getattr(hclsm_module, "dynamics", None)
+    obj = getattr(hclsm_module, "objects", None)
+    l0 = getattr(dyn, "level0_ssm", None) if dyn is not None else None
+    if l0 is not None and hasattr(l0, "SimplifiedSSMBlock"):
+        _patch(l0.SimplifiedSSMBlock, "forward", _ssm_block_forward)
+        done.append("SimplifiedSSMBlock.forward")
+    ds = getattr(obj, "dynamic_slots", None) if obj is not None else None
+    if ds is not None and hasattr(ds, "DynamicSlotAttention"):
+        cls = ds.DynamicSlotAttention
+        _patch(cls, "_iteration_step", _make_iteration_step(_orig(cls, "_iteration_step")))
+        done.append("DynamicSlotAttention._iteration_step")
+    hm = getattr(dyn, "hierarchy_manager", None) if dyn is not None else None
+    if hm is not None and hasattr(hm, "HierarchyManager"):
+        cls = hm.HierarchyManager
+        _patch(cls, "gather_events", _make_gather(_orig(cls, "gather_events")))
+        _patch(cls, "scatter_events", _make_scatter(_orig(cls, "scatter_events")))
+        done += ["HierarchyManager.gather_events", "HierarchyManager.scatter_events"]
+    l1 = getattr(dyn, "level1_event", None) if dyn is not None else None
+    if l1 is not None and hasattr(l1, "Level1EventDynamics"):
+        cls = l1.Level1EventDynamics
+        _patch(cls, "forward", _make_level1_forward(_orig(cls, "forward")))
+        done.append("Level1EventDynamics.forward")
+    return done

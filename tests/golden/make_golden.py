@@ -94,6 +94,32 @@ def _scan_case(sk, name, x, dt, A_log, Bp, C, dy, Dv=None, z=None):
     return o
 
 
+def block_cases():
+    """SimplifiedSSMBlock forward and input/parameter gradients
+    (hclsm/dynamics/level0_ssm.py:30-107), weights drawn so the clamps bind."""
+    from hclsm.dynamics.level0_ssm import SimplifiedSSMBlock
+
+    g = torch.Generator().manual_seed(500)
+    blk = SimplifiedSSMBlock(d_model=32, d_state=16)
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if name.startswith("norm"):
+                continue
+            if name == "A_log":
+                p.copy_(torch.empty(p.shape).uniform_(-1.0, 0.5, generator=g))  # some exp(A_log) > 1: clamp binds
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.3)
+    x = torch.randn(6, 12, 32, generator=g, requires_grad=True)
+    dy = torch.randn(6, 12, 32, generator=g)
+    y = blk(x)
+    y.backward(dy)
+    out = {"blk/x": _np(x), "blk/dy": _np(dy), "blk/y": _np(y), "blk/dx": _np(x.grad)}
+    for name, p in blk.named_parameters():
+        out[f"blk/w/{name}"] = _np(p)
+        out[f"blk/g/{name}"] = _np(p.grad)
+    return out
+
+
 def slot_cases():
     from hclsm.kernels.slot_attention_kernel import naive_slot_attention
     from hclsm.config import ObjectConfig
@@ -185,7 +211,7 @@ def main():
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(1)
-    np.savez_compressed(os.path.join(HERE, "scan_golden.npz"), **scan_cases())
+    np.savez_compressed(os.path.join(HERE, "scan_golden.npz"), **scan_cases(), **block_cases())
     np.savez_compressed(os.path.join(HERE, "slot_golden.npz"), **slot_cases())
     np.savez_compressed(os.path.join(HERE, "event_golden.npz"), **event_cases())
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
