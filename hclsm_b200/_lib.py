@@ -34,6 +34,7 @@ _sz = ctypes.c_size_t
 SIGNATURES = {
     "hclsm_version": (ctypes.c_int, []),
     "hclsm_device_error": (ctypes.c_int, []),
+    "hclsm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, _vp, _vp]),
     "hclsm_ssm_scan_fwd": (ctypes.c_int, [_vp] * 8 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "hclsm_ssm_scan_bwd_workspace_size": (_sz, [_i64, _i32, _i32, _i32]),
     "hclsm_ssm_scan_bwd": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),

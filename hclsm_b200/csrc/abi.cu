@@ -61,3 +61,36 @@ extern "C" int hclsm_device_error(void) {
   cudaMemcpyToSymbol(g_hclsm_err, &zero, sizeof(int));
   return v;
 }
+
+namespace {
+// Waits on an mbarrier that nothing ever completes, at most `polls` times, then
+// records HCLSM_ERR_TIMEOUT and returns: the bounded-wait path every kernel of
+// this library uses, exercised without a fault.
+__global__ void selftest_wait_kernel(uint32_t polls, int* err, int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    hclsm::mbar_init(&bar, 1);
+    hclsm::fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t addr = hclsm::smem_u32(&bar);
+  uint32_t done = 0;
+  for (uint32_t i = 0; i < polls && !done; ++i) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(0u)
+        : "memory");
+  }
+  if (threadIdx.x == 0) {
+    *status = done ? 0 : HCLSM_ERR_TIMEOUT;
+    if (!done) hclsm::record_error(err, HCLSM_ERR_TIMEOUT);
+  }
+}
+}  // namespace
+
+extern "C" int hclsm_selftest_wait_timeout(uint32_t polls, int* status_dev, void* stream) {
+  if (!status_dev) return HCLSM_ERR_NULL;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(polls, hclsm::device_err_ptr(), status_dev);
+  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}

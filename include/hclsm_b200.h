@@ -46,6 +46,11 @@ typedef enum { HCLSM_F32 = 0, HCLSM_BF16 = 1 } hclsm_dtype;
 int hclsm_version(void);
 int hclsm_device_error(void);
 
+/* Self-test of the bounded device-side wait (no reference counterpart): one
+ * block polls an mbarrier that nothing completes `polls` times, then writes
+ * HCLSM_ERR_TIMEOUT to *status_dev (device int) and to the error word. */
+int hclsm_selftest_wait_timeout(uint32_t polls, int* status_dev, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Selective SSM scan, forward.
  * Replaces hclsm/kernels/ssm_scan_kernel.py:394 ssm_scan_fn (the dispatcher),
