@@ -159,22 +159,17 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdParams p) {
 
 // Forward, bf16 I/O, two adjacent channels per thread (the bf16x2 word of x,
 // dt, z and y).  The channel pair is processed with packed arithmetic:
-//   arg  = dt2 * A2  (f16x2)       one HMUL2 for both channels
-//   dA   = 2^arg     (f16x2)       one MUFU op for two exponentials
+//   arg  = dt2 * A2                fp32 pair (FMUL2)
+//   dA   = 2^arg                   two ex2.approx.f32 (SFU)
 //   h    = fma2(dA, h, dt*x*B)     fp32 pairs (FFMA2), state stays fp32
 //   y   += h * C                   fp32 pairs (FFMA2)
-// The f16 exponential carries a relative error of ~1e-3 on dA; states and
-// accumulation stay fp32, well inside the 2e-2 budget of the bf16 configs.
+// (An f16x2 exponential halves the SFU ops but its f16 -> f32 conversions cost
+// more than that on sm_100a: measured 19.9 vs 18.4 ms at config 4.)
 // x/dt/z are prefetched one 4-step block ahead in registers; B and C of 64
 // steps are staged in shared memory as duplicated pairs (B, B) so that one
 // 64-bit load yields an FFMA2 operand.
 constexpr int kFwdBlk = 4;
 
-__device__ __forceinline__ __half2 ex2_h2(__half2 v) {
-  uint32_t r, a = *reinterpret_cast<uint32_t*>(&v);
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(a));
-  return *reinterpret_cast<__half2*>(&r);
-}
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
@@ -200,7 +195,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
   const __nv_bfloat16* __restrict__ Cm = static_cast<const __nv_bfloat16*>(p.C);
   const bool has_z = z != nullptr;
 
-  __half2 A2[SP];
+  float2 A2[SP];
   float2 h[SP];
 #pragma unroll
   for (int s = 0; s < SP; ++s) {
@@ -215,7 +210,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
       a0 = -e0 * kLog2e;
       a1 = -e1 * kLog2e;
     }
-    A2[s] = __floats2half2_rn(a0, a1);
+    A2[s] = make_float2(a0, a1);
     h[s] = make_float2(0.0f, 0.0f);
   }
   const float2 Dv = (p.Dp && act) ? make_float2(p.Dp[d0], p.Dp[d0 + 1]) : make_float2(0.0f, 0.0f);
@@ -262,11 +257,11 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
             dv.y = fminf(fmaxf(dv.y, 1e-3f), 1.0f);
           }
           const float2 dtx = __fmul2_rn(dv, xv);
-          const __half2 dth = __floats2half2_rn(dv.x, dv.y);
           float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
           for (int s = 0; s < SP; ++s) {
-            const float2 dA = __half22float2(ex2_h2(__hmul2(dth, A2[s])));
+            const float2 ar = __fmul2_rn(dv, A2[s]);
+            const float2 dA = make_float2(ex2(ar.x), ex2(ar.y));
             h[s] = __ffma2_rn(dA, h[s], __fmul2_rn(dtx, sB[tt][s]));
             acc = __ffma2_rn(h[s], sC[tt][s], acc);
           }
@@ -761,8 +756,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
 //  * the sqrt(L) checkpoints of h (every 10 steps) live in a per-SM slot of
 //    the workspace (blocks run one per SM, slot = %smid), which stays resident
 //    in L2; the next chunk's checkpoint is fetched while a chunk is processed;
-//  * per-state arithmetic runs on state pairs (FFMA2 / FMUL2); exp(dt*A) is one
-//    f16x2 SFU op per pair;
+//  * per-state arithmetic runs on state pairs (FFMA2 / FMUL2); exp(dt*A) is
+//    ex2.approx.f32, and dA is parked as f16x2 (one pack per pair) so that 10
+//    steps fit the TMEM half (fp32 dA, 8-step chunks, measured slower);
 //  * in the dB/dC warp reduction, lane l keeps state s in register slot
 //    s ^ (l & 12), so the levels that exchange across lane bits 3 and 2 keep
 //    slots [0, n/2) without selects.
@@ -935,7 +931,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     const int d = g * kW16Ch + tid;
     const bool act = d < D;
     float2 A[8];
-    __half2 A2[8];
+    float2 A2[8];
     float fac[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -951,7 +947,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       if (j & 1) A[j >> 1].y = a; else A[j >> 1].x = a;
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) A2[q] = __floats2half2_rn(A[q].x * kLog2e, A[q].y * kLog2e);
+    for (int q = 0; q < 8; ++q) A2[q] = f2(A[q].x * kLog2e, A[q].y * kLog2e);
     const float Dd = (has_D && act) ? p.Dp[d] : 0.0f;
 
     // ---- forward sweep: checkpoints (to this SM's L2-resident slot) ------------
@@ -974,12 +970,13 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float2 dtx = f2(dv * xv, dv * xv);
-        const __half2 dth = __float2half2_rn(dv);
+        const float2 dvv2 = f2(dv, dv);
         float2 Bt[8];
         load_bc(sBf, t0 + j, Bt);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float2 dA = __half22float2(ex2_h2(__hmul2(dth, A2[q])));
+          const float2 ar = __fmul2_rn(dvv2, A2[q]);
+          const float2 dA = f2(ex2(ar.x), ex2(ar.y));
           h[q] = __ffma2_rn(dA, h[q], __fmul2_rn(dtx, Bt[q]));
         }
       }
@@ -1021,14 +1018,16 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float2 dtx = f2(dv * xv, dv * xv);
-        const __half2 dth = __float2half2_rn(dv);
+        const float2 dvv2 = f2(dv, dv);
         float2 Bt[8];
         load_bc(sBf, t0 + j, Bt);
         float hv[16], dw[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const __half2 e = ex2_h2(__hmul2(dth, A2[q]));
-          hs[q] = __ffma2_rn(__half22float2(e), hs[q], __fmul2_rn(dtx, Bt[q]));
+          const float2 ar = __fmul2_rn(dvv2, A2[q]);
+          const float2 ef = f2(ex2(ar.x), ex2(ar.y));
+          const __half2 e = __floats2half2_rn(ef.x, ef.y);
+          hs[q] = __ffma2_rn(ef, hs[q], __fmul2_rn(dtx, Bt[q]));
           hv[2 * q] = hs[q].x;
           hv[2 * q + 1] = hs[q].y;
           dw[q] = __uint_as_float(h2_bits(e));
