@@ -66,7 +66,7 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
 }
 
 // Shared memory: Q (NP rows), K chunk, V chunk (kChunk rows each, row stride
-// D + kPad), attn chunk [NP][kChunk + kPad], one mbarrier.
+// D + kPad), attn chunk [NP][kChunk + kPad], two mbarriers (K, V).
 struct CoreSmem {
   static __host__ __device__ size_t row(int D) { return (size_t)(D + kPad) * 2; }
   static __host__ __device__ size_t q_off() { return 0; }
@@ -74,7 +74,7 @@ struct CoreSmem {
   static __host__ __device__ size_t v_off(int NP, int D) { return k_off(NP, D) + kChunk * row(D); }
   static __host__ __device__ size_t a_off(int NP, int D) { return v_off(NP, D) + kChunk * row(D); }
   static __host__ __device__ size_t bar_off(int NP, int D) { return a_off(NP, D) + (size_t)NP * (kChunk + kPad) * 2; }
-  static __host__ __device__ size_t total(int NP, int D) { return bar_off(NP, D) + 16; }
+  static __host__ __device__ size_t total(int NP, int D) { return bar_off(NP, D) + 32; }
 };
 
 // NM: 16-slot tiles (N <= 16*NM); NT: 8-column output tiles per warp (D <= 64*NT)
@@ -96,29 +96,32 @@ __global__ void __launch_bounds__(kThreads, 1) core_bf16_kernel(CoreParams p) {
   const __nv_bfloat16* gV = static_cast<const __nv_bfloat16*>(p.V) + (size_t)f * M * D;
   const uint32_t row_bytes = (uint32_t)D * 2;
 
-  // Q rows (padded slots zero) through the bulk engine, together with chunk 0
+  // Q rows (padded slots zero) arrive with chunk 0's K rows.  K and V of a chunk
+  // have separate barriers: chunk c+1's K rows load while chunk c's attn^T V
+  // runs, its V rows while chunk c+1's logits run.
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_mbar_init();
   }
   for (int i = tid; i < (NP - N) * (D + kPad); i += kThreads)
     reinterpret_cast<__nv_bfloat16*>(sQ + (size_t)N * RB)[i] = __float2bfloat16_rn(0.0f);
   __syncthreads();
-  auto issue_chunk = [&](int m0, bool with_q) {
+  auto issue_rows = [&](int which, int m0, bool with_q) {  // which: 0 = K (+Q), 1 = V
     const int rows = min(kChunk, M - m0);
     if (warp == 0) {
-      if (lane == 0)
-        mbar_expect_tx(bar, row_bytes * (2 * rows + (with_q ? N : 0)));
+      if (lane == 0) mbar_expect_tx(&bar[which], row_bytes * (rows + (with_q ? N : 0)));
       __syncwarp();
-      for (int r = lane; r < rows; r += 32) {
-        bulk_g2s(sK + (size_t)r * RB, gK + (size_t)(m0 + r) * D, row_bytes, bar);
-        bulk_g2s(sV + (size_t)r * RB, gV + (size_t)(m0 + r) * D, row_bytes, bar);
-      }
+      unsigned char* dst = which == 0 ? sK : sV;
+      const __nv_bfloat16* src = which == 0 ? gK : gV;
+      for (int r = lane; r < rows; r += 32)
+        bulk_g2s(dst + (size_t)r * RB, src + (size_t)(m0 + r) * D, row_bytes, &bar[which]);
       if (with_q)
-        for (int r = lane; r < N; r += 32) bulk_g2s(sQ + (size_t)r * RB, gQ + (size_t)r * D, row_bytes, bar);
+        for (int r = lane; r < N; r += 32) bulk_g2s(sQ + (size_t)r * RB, gQ + (size_t)r * D, row_bytes, &bar[0]);
     }
   };
-  issue_chunk(0, true);
+  issue_rows(0, 0, true);
+  issue_rows(1, 0, false);
 
   float acc[NM][NT][4];
 #pragma unroll
@@ -133,17 +136,17 @@ __global__ void __launch_bounds__(kThreads, 1) core_bf16_kernel(CoreParams p) {
   const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV), sAa = smem_u32(sA);
   constexpr int AR = kChunk + kPad;  // attn row stride (elements)
   int phase = 0;
+  auto zero_tail = [&](unsigned char* buf, int rows) {
+    for (int i = tid; i < (kChunk - rows) * (D / 2); i += kThreads) {
+      const int r = rows + i / (D / 2), c = i % (D / 2);
+      reinterpret_cast<uint32_t*>(buf + (size_t)r * RB)[c] = 0u;
+    }
+  };
   for (int m0 = 0; m0 < M; m0 += kChunk) {
     const int rows = min(kChunk, M - m0);
-    if (!mbar_wait(bar, phase)) record_error(p.err, HCLSM_ERR_TIMEOUT);
-    phase ^= 1;
-    // zero K/V rows past the end of the token range
-    if (rows < kChunk) {
-      for (int i = tid; i < (kChunk - rows) * (D / 2); i += kThreads) {
-        const int r = rows + i / (D / 2), c = i % (D / 2);
-        reinterpret_cast<uint32_t*>(sK + (size_t)r * RB)[c] = 0u;
-        reinterpret_cast<uint32_t*>(sV + (size_t)r * RB)[c] = 0u;
-      }
+    if (!mbar_wait(&bar[0], phase)) record_error(p.err, HCLSM_ERR_TIMEOUT);
+    if (rows < kChunk) {  // K rows past the end of the token range
+      zero_tail(sK, rows);
       __syncthreads();
     }
     // ---- phase 1: logits for 16 tokens x NP slots per warp ---------------------
@@ -211,6 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1) core_bf16_kernel(CoreParams p) {
       }
     }
     __syncthreads();
+    // sK is free: fetch the next chunk's K rows during this chunk's attn^T V
+    if (m0 + kChunk < M) issue_rows(0, m0 + kChunk, false);
+    if (!mbar_wait(&bar[1], phase)) record_error(p.err, HCLSM_ERR_TIMEOUT);
+    if (rows < kChunk) {
+      zero_tail(sV, rows);
+      __syncthreads();
+    }
     // ---- phase 2: out += attn^T * V for this warp's column tiles ---------------
     for (int k0 = 0; k0 < kChunk; k0 += 16) {
       uint32_t af[NM][4];
@@ -230,7 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1) core_bf16_kernel(CoreParams p) {
       }
     }
     __syncthreads();
-    if (m0 + kChunk < M) issue_chunk(m0 + kChunk, false);
+    if (m0 + kChunk < M) issue_rows(1, m0 + kChunk, false);
+    phase ^= 1;
   }
   // ---- epilogue -------------------------------------------------------------------
   __nv_bfloat16* gO = static_cast<__nv_bfloat16*>(p.out) + (size_t)f * N * D;
@@ -333,21 +344,42 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
 }
 
 // torch.nn.GRUCell: gate rows ordered (r, z, n).  gi = x W_ih^T, gh = h W_hh^T
-// (fp32, without biases); h_out = (1 - z) * n + z * h.
+// (fp32, without biases); h_out = (1 - z) * n + z * h.  Four columns per
+// thread (C % 4 == 0, checked by the host).
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
 __global__ void gru_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
                            const float* __restrict__ b_ih, const float* __restrict__ b_hh,
                            const float* __restrict__ h, float* __restrict__ h_out, int64_t rows, int H) {
-  const int64_t total = rows * H;
+  const int Q = H / 4;
+  const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / H;
-    const int c = (int)(i % H);
+    const int64_t r = i / Q;
+    const int c = (int)(i % Q) * 4;
     const float* gir = gi + r * 3 * H;
     const float* ghr = gh + r * 3 * H;
-    const float rg = sigmoid(gir[c] + b_ih[c] + ghr[c] + b_hh[c]);
-    const float zg = sigmoid(gir[H + c] + b_ih[H + c] + ghr[H + c] + b_hh[H + c]);
-    const float pre = gir[2 * H + c] + b_ih[2 * H + c] + rg * (ghr[2 * H + c] + b_hh[2 * H + c]);
-    const float ng = 2.0f * sigmoid(2.0f * pre) - 1.0f;  // tanh
-    h_out[i] = (1.0f - zg) * ng + zg * h[i];
+    const float4 ir = ld4(gir + c), iz = ld4(gir + H + c), in = ld4(gir + 2 * H + c);
+    const float4 hr = ld4(ghr + c), hz = ld4(ghr + H + c), hn = ld4(ghr + 2 * H + c);
+    const float4 bir = ld4(b_ih + c), biz = ld4(b_ih + H + c), bin = ld4(b_ih + 2 * H + c);
+    const float4 bhr = ld4(b_hh + c), bhz = ld4(b_hh + H + c), bhn = ld4(b_hh + 2 * H + c);
+    const float4 hv = ld4(h + r * H + c);
+    float o[4];
+    const float a_ir[4] = {ir.x, ir.y, ir.z, ir.w}, a_iz[4] = {iz.x, iz.y, iz.z, iz.w}, a_in[4] = {in.x, in.y, in.z, in.w};
+    const float a_hr[4] = {hr.x, hr.y, hr.z, hr.w}, a_hz[4] = {hz.x, hz.y, hz.z, hz.w}, a_hn[4] = {hn.x, hn.y, hn.z, hn.w};
+    const float b_r[4] = {bir.x + bhr.x, bir.y + bhr.y, bir.z + bhr.z, bir.w + bhr.w};
+    const float b_z[4] = {biz.x + bhz.x, biz.y + bhz.y, biz.z + bhz.z, biz.w + bhz.w};
+    const float b_in[4] = {bin.x, bin.y, bin.z, bin.w}, b_hn[4] = {bhn.x, bhn.y, bhn.z, bhn.w};
+    const float a_h[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float rg = sigmoid(a_ir[k] + a_hr[k] + b_r[k]);
+      const float zg = sigmoid(a_iz[k] + a_hz[k] + b_z[k]);
+      const float pre = a_in[k] + b_in[k] + rg * (a_hn[k] + b_hn[k]);
+      const float ng = 2.0f * sigmoid(2.0f * pre) - 1.0f;  // tanh
+      o[k] = (1.0f - zg) * ng + zg * a_h[k];
+    }
+    st4(h_out + r * H + c, make_float4(o[0], o[1], o[2], o[3]));
   }
 }
 
@@ -355,11 +387,27 @@ __global__ void gru_kernel(const float* __restrict__ gi, const float* __restrict
 template <typename TO>
 __global__ void bias_act_kernel(const float* __restrict__ x, const float* __restrict__ b, TO* __restrict__ y,
                                 int64_t rows, int C, int act) {
-  const int64_t total = rows * C;
+  const int Q = C / 4;
+  const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    float v = x[i] + (b ? b[i % C] : 0.0f);
-    if (act == 1) v = fmaxf(v, 0.0f);
-    io<TO>::st(y + i, v);
+    const int c = (int)(i % Q) * 4;
+    float4 v = ld4(x + i * 4);
+    if (b) {
+      const float4 bb = ld4(b + c);
+      v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+    }
+    if (act == 1) {
+      v.x = fmaxf(v.x, 0.0f); v.y = fmaxf(v.y, 0.0f); v.z = fmaxf(v.z, 0.0f); v.w = fmaxf(v.w, 0.0f);
+    }
+    if constexpr (sizeof(TO) == 2) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+      uint2 w;
+      w.x = *reinterpret_cast<uint32_t*>(&lo);
+      w.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(y + i * 4) = w;
+    } else {
+      st4(reinterpret_cast<float*>(y) + i * 4, v);
+    }
   }
 }
 
@@ -367,12 +415,28 @@ __global__ void bias_act_kernel(const float* __restrict__ x, const float* __rest
 __global__ void residual_clamp_kernel(const float* __restrict__ h, const float* __restrict__ m,
                                       const float* __restrict__ b, float* __restrict__ out,
                                       __nv_bfloat16* __restrict__ out_bf16, int64_t rows, int C, float c) {
-  const int64_t total = rows * C;
+  const int Q = C / 4;
+  const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    float v = h[i] + m[i] + (b ? b[i % C] : 0.0f);
-    if (c > 0.0f) v = fminf(fmaxf(v, -c), c);
-    out[i] = v;
-    if (out_bf16) out_bf16[i] = __float2bfloat16_rn(v);
+    const int col = (int)(i % Q) * 4;
+    const float4 hv = ld4(h + i * 4), mv = ld4(m + i * 4);
+    float v[4] = {hv.x + mv.x, hv.y + mv.y, hv.z + mv.z, hv.w + mv.w};
+    if (b) {
+      const float4 bb = ld4(b + col);
+      v[0] += bb.x; v[1] += bb.y; v[2] += bb.z; v[3] += bb.w;
+    }
+    if (c > 0.0f) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = fminf(fmaxf(v[k], -c), c);
+    }
+    st4(out + i * 4, make_float4(v[0], v[1], v[2], v[3]));
+    if (out_bf16) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+      uint2 w;
+      w.x = *reinterpret_cast<uint32_t*>(&lo);
+      w.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(out_bf16 + i * 4) = w;
+    }
   }
 }
 
@@ -467,8 +531,9 @@ extern "C" int hclsm_gru_cell(const float* gi, const float* gh, const float* b_i
                               const float* h, float* h_out, int64_t rows, int32_t H, void* stream) {
   if (!gi || !gh || !b_ih || !b_hh || !h || !h_out) return HCLSM_ERR_NULL;
   if (rows < 0 || H <= 0) return HCLSM_ERR_SHAPE;
+  if (H % 4) return HCLSM_ERR_UNSUPPORTED;
   if (rows == 0) return HCLSM_OK;
-  gru_kernel<<<ew_blocks(rows * H), 256, 0, static_cast<cudaStream_t>(stream)>>>(gi, gh, b_ih, b_hh, h, h_out,
+  gru_kernel<<<ew_blocks(rows * H / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(gi, gh, b_ih, b_hh, h, h_out,
                                                                                  rows, H);
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
 }
@@ -477,13 +542,14 @@ extern "C" int hclsm_bias_act(const float* x, const float* b, void* y, int64_t r
                               int32_t out_dtype, void* stream) {
   if (!x || !y) return HCLSM_ERR_NULL;
   if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
+  if (C % 4) return HCLSM_ERR_UNSUPPORTED;
   if (rows == 0) return HCLSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (out_dtype == HCLSM_BF16)
-    bias_act_kernel<__nv_bfloat16><<<ew_blocks(rows * C), 256, 0, st>>>(x, b, static_cast<__nv_bfloat16*>(y), rows,
+    bias_act_kernel<__nv_bfloat16><<<ew_blocks(rows * C / 4), 256, 0, st>>>(x, b, static_cast<__nv_bfloat16*>(y), rows,
                                                                         C, act);
   else if (out_dtype == HCLSM_F32)
-    bias_act_kernel<float><<<ew_blocks(rows * C), 256, 0, st>>>(x, b, static_cast<float*>(y), rows, C, act);
+    bias_act_kernel<float><<<ew_blocks(rows * C / 4), 256, 0, st>>>(x, b, static_cast<float*>(y), rows, C, act);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -493,8 +559,9 @@ extern "C" int hclsm_residual_clamp(const float* h, const float* m, const float*
                                     int64_t rows, int32_t C, float clamp, void* stream) {
   if (!h || !m || !out) return HCLSM_ERR_NULL;
   if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
+  if (C % 4) return HCLSM_ERR_UNSUPPORTED;
   if (rows == 0) return HCLSM_OK;
-  residual_clamp_kernel<<<ew_blocks(rows * C), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  residual_clamp_kernel<<<ew_blocks(rows * C / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       h, m, b, out, static_cast<__nv_bfloat16*>(out_bf16), rows, C, clamp);
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
 }
