@@ -743,6 +743,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
   }
 }
 
+// TMEM loads whose destination registers are tied to the wait: the values are
+// consumed only after tcgen05.wait::ld, and no memory clobber is needed, so
+// shared-memory traffic can be scheduled across them.
+__device__ __forceinline__ void tmem_ld16_nc(uint32_t taddr, float (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15}, [%16];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]),
+        "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]), "=f"(v[14]), "=f"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8_nc(uint32_t taddr, float (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld_tied(float (&a)[16], float (&b)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]), "+f"(a[5]), "+f"(a[6]), "+f"(a[7]),
+                 "+f"(a[8]), "+f"(a[9]), "+f"(a[10]), "+f"(a[11]), "+f"(a[12]), "+f"(a[13]), "+f"(a[14]),
+                 "+f"(a[15]), "+f"(b[0]), "+f"(b[1]), "+f"(b[2]), "+f"(b[3]), "+f"(b[4]), "+f"(b[5]), "+f"(b[6]),
+                 "+f"(b[7]));
+}
+
 // ---------------------------------------------------------------------------
 // backward, bf16 I/O and d_state <= 16: packed variant, 8 warps
 // ---------------------------------------------------------------------------
@@ -1040,13 +1064,13 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       float nh[16], nd[8];
       {
         const uint32_t col = tmem + (uint32_t)((n - 1) * kW16Cols);
-        tmem_ld8(col + 16, nd);
-        if (n - 1 > 0) tmem_ld16(col - kW16Cols, nh);
+        tmem_ld8_nc(col + 16, nd);
+        if (n - 1 > 0) tmem_ld16_nc(col - kW16Cols, nh);
       }
 #pragma unroll 2
       for (int j = n - 1; j >= 0; --j) {
         const int t = t0 + j;
-        tmem_wait_ld();
+        tmem_wait_ld_tied(nh, nd);
         float2 hp[8];
         uint32_t dwv[8];
         if (j > 0) {
@@ -1060,8 +1084,8 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         for (int q = 0; q < 8; ++q) dwv[q] = __float_as_uint(nd[q]);
         if (j > 0) {
           const uint32_t col = tmem + (uint32_t)((j - 1) * kW16Cols);
-          tmem_ld8(col + 16, nd);
-          if (j - 1 > 0) tmem_ld16(col - kW16Cols, nh);
+          tmem_ld8_nc(col + 16, nd);
+          if (j - 1 > 0) tmem_ld16_nc(col - kW16Cols, nh);
         }
         const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
         const float draw = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
