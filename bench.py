@@ -180,7 +180,8 @@ def run_b200(args, rank, world, local_rank):
 def run_e2e(args, rank, world, dev):
     """Inputs in pinned host memory; per step: H2D copy, forward + backward via
     ``ssm_scan_fn`` and autograd, D2H copy of y and every gradient.  Chunks of
-    sequences are pipelined over a copy stream and the compute stream."""
+    sequences are pipelined over an upload stream, the compute stream and a
+    download stream, so both PCIe directions run at once."""
     import torch
     import torch.distributed as dist
 
@@ -195,17 +196,18 @@ def run_e2e(args, rank, world, dev):
     dA_host = torch.empty(DI, DS, dtype=torch.float32).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = sum(v.numel() * v.element_size() for v in outs.values()) + dA_host.numel() * 4
-    cs = torch.cuda.Stream(dev)
+    up = torch.cuda.Stream(dev)    # host -> device
+    down = torch.cuda.Stream(dev)  # device -> host (the other PCIe direction)
     comp = torch.cuda.current_stream(dev)
 
     def step():
         A = host["A_log"].to(dev, non_blocking=True).requires_grad_(True)
         for s0 in range(0, n, chunk):
             s1 = min(n, s0 + chunk)
-            with torch.cuda.stream(cs):
+            with torch.cuda.stream(up):
                 dv = {k: host[k][s0:s1].to(dev, non_blocking=True) for k in ("x", "dt", "B", "C", "dy")}
                 ready = torch.cuda.Event()
-                ready.record(cs)
+                ready.record(up)
             comp.wait_event(ready)
             for v in dv.values():
                 v.record_stream(comp)
@@ -214,13 +216,13 @@ def run_e2e(args, rank, world, dev):
             torch.autograd.backward(y, dv["dy"])
             done = torch.cuda.Event()
             done.record(comp)
-            with torch.cuda.stream(cs):
-                cs.wait_event(done)
+            with torch.cuda.stream(down):
+                down.wait_event(done)
                 for k, t in (("y", y), ("dx", leaves[0].grad), ("ddt", leaves[1].grad),
                              ("dB", leaves[2].grad), ("dC", leaves[3].grad)):
                     outs[k][s0:s1].copy_(t.detach(), non_blocking=True)
-                    t.record_stream(cs)
-        comp.wait_stream(cs)
+                    t.record_stream(down)
+        comp.wait_stream(down)
         dA_host.copy_(A.grad, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
