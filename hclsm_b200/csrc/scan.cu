@@ -322,19 +322,32 @@ struct BwdParams {
   int* err;
 };
 
-// Host and device agree on this shared-memory layout.
+// Host and device agree on this shared-memory layout: tile stages, one chunk
+// of B and C (fp32), the per-chunk dB|dC slab, barriers.  Checkpoints live in
+// the workspace (one slot per SM).  The total is padded past half of the SM's
+// shared memory so that one block runs per SM (the slots rely on it).
 template <typename T, int SP>
 struct BwdSmem {
   using Cfg = BwdCfg<T, SP>;
   __host__ __device__ static size_t tiles_off() { return 0; }
   __host__ __device__ static size_t bc_off() { return Cfg::NSTAGE * Cfg::stage_bytes; }
-  __host__ __device__ static size_t slab_off(int L) { return bc_off() + (size_t)L * SP * 2 * sizeof(float); }
-  __host__ __device__ static size_t ckpt_off(int L) { return slab_off(L) + 4 * (size_t)Cfg::K * Cfg::NV * sizeof(float); }
-  __host__ __device__ static size_t bar_off(int L, int nck) {
-    return ckpt_off(L) + (size_t)(nck > 1 ? nck - 1 : 0) * SP * kBwdThreads * sizeof(float);
+  __host__ __device__ static size_t slab_off() { return bc_off() + (size_t)Cfg::K * SP * 2 * sizeof(float); }
+  __host__ __device__ static size_t bar_off() { return slab_off() + 4 * (size_t)Cfg::K * Cfg::NV * sizeof(float); }
+  __host__ __device__ static size_t total() {
+    const size_t t = bar_off() + 64;
+    return t > 120 * 1024 ? t : 120 * 1024;
   }
-  __host__ __device__ static size_t total(int L, int nck) { return bar_off(L, nck) + 64; }
 };
+// checkpoint floats per SM slot of the generic kernel
+__host__ __device__ inline size_t gen_slot_floats(int nck, int SP) {
+  return (size_t)(nck > 1 ? nck - 1 : 0) * SP * 128;
+}
+
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
@@ -466,14 +479,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
   const int split = blockIdx.y;
   const int g_begin = split * p.groups_per_cta;
   const int g_end = min(p.groups, g_begin + p.groups_per_cta);
-  if (g_begin >= g_end) return;  // uniform across the CTA
+  if (g_begin >= g_end) {  // no channels for this split: its dB|dC rows are zero
+    float* dst = p.dBC_ws + ((int64_t)split * p.nseq + b) * L * NV;
+    for (int e = tid; e < L * NV; e += kBwdThreads) dst[e] = 0.0f;
+    return;
+  }
+  const uint32_t slot = smid();
+  if (slot >= (uint32_t)p.ckpt_slots) {
+    if (tid == 0) record_error(p.err, HCLSM_ERR_LAUNCH);
+    return;
+  }
 
   T* tiles = reinterpret_cast<T*>(smem + Sm::tiles_off());
-  float* sBf = reinterpret_cast<float*>(smem + Sm::bc_off());  // (L, SP)
-  float* sCf = sBf + (size_t)L * SP;                             // (L, SP)
-  float* slab = reinterpret_cast<float*>(smem + Sm::slab_off(L));  // (4, K, NV)
-  float4* ckpt = reinterpret_cast<float4*>(smem + Sm::ckpt_off(L));  // (nck-1, SP/4, 128)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bar_off(L, nck));
+  float* sBf = reinterpret_cast<float*>(smem + Sm::bc_off());  // (K, SP): this chunk's B
+  float* sCf = sBf + (size_t)K * SP;                             // (K, SP): this chunk's C
+  float* slab = reinterpret_cast<float*>(smem + Sm::slab_off());  // (4, K, NV)
+  float4* ckpt = reinterpret_cast<float4*>(p.ckpt_ws + (size_t)slot * gen_slot_floats(nck, SP));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Sm::bar_off());
+  const T* Bseq = static_cast<const T*>(p.B) + b * L * S;
+  const T* Cseq = static_cast<const T*>(p.C) + b * L * S;
+  // stage B and C of steps [t0, t0 + n) as fp32 (padded states zero)
+  auto stage_bc = [&](int t0, int n) {
+    __syncthreads();
+    for (int i = tid; i < n * SP; i += kBwdThreads) {
+      const int t = i / SP, s = i % SP;
+      sBf[i] = s < S ? io<T>::ld(Bseq + (int64_t)(t0 + t) * S + s) : 0.0f;
+      sCf[i] = s < S ? io<T>::ld(Cseq + (int64_t)(t0 + t) * S + s) : 0.0f;
+    }
+    __syncthreads();
+  };
 
   const T* __restrict__ gx = static_cast<const T*>(p.x);
   const T* __restrict__ gdt = static_cast<const T*>(p.dt);
@@ -494,15 +528,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
     s_abort = 0;
     for (int i = 0; i < NSTAGE; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
-  }
-  {
-    const T* Bm = static_cast<const T*>(p.B) + b * L * S;
-    const T* Cm = static_cast<const T*>(p.C) + b * L * S;
-    for (int i = tid; i < L * SP; i += kBwdThreads) {
-      const int t = i / SP, s = i % SP;
-      sBf[i] = s < S ? io<T>::ld(Bm + (int64_t)t * S + s) : 0.0f;
-      sCf[i] = s < S ? io<T>::ld(Cm + (int64_t)t * S + s) : 0.0f;
-    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -579,18 +604,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
       wait_item(it);
       const T* st = tiles + (size_t)(it % NSTAGE) * Cfg::NTEN * Cfg::tile_elems;
       const int t0 = k * K, n = min(K, L - t0);
+      stage_bc(t0, n);
       if (k > 0) {
 #pragma unroll
         for (int q = 0; q < SP / 4; ++q)
-          ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid] =
-              make_float4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+          __stcg(&ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid],
+                 make_float4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]));
       }
       for (int j = 0; j < n; ++j) {
         float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
         float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float dtx = dv * xv;
-        const float* Bt = sBf + (size_t)(t0 + j) * SP;
+        const float* Bt = sBf + (size_t)j * SP;
 #pragma unroll
         for (int s = 0; s < SP; ++s) h[s] = fmaf(ex2(dv * A2[s]), h[s], dtx * Bt[s]);
       }
@@ -607,12 +633,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
       wait_item(it);
       const T* st = tiles + (size_t)(it % NSTAGE) * Cfg::NTEN * Cfg::tile_elems;
       const int t0 = k * K, n = min(K, L - t0);
+      stage_bc(t0, n);
       // recompute the chunk from its checkpoint, parking h_t and dA_t in TMEM
       float hs[SP];
       if (k > 0) {
 #pragma unroll
         for (int q = 0; q < SP / 4; ++q) {
-          const float4 c4 = ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid];
+          const float4 c4 = __ldcg(&ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid]);
           hs[4 * q] = c4.x; hs[4 * q + 1] = c4.y; hs[4 * q + 2] = c4.z; hs[4 * q + 3] = c4.w;
         }
       } else {
@@ -624,7 +651,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
         float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float dtx = dv * xv;
-        const float* Bt = sBf + (size_t)(t0 + j) * SP;
+        const float* Bt = sBf + (size_t)j * SP;
         float dA[SP];
 #pragma unroll
         for (int s = 0; s < SP; ++s) {
@@ -648,8 +675,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
           dv = fminf(fmaxf(draw, 1e-3f), 1.0f);
         }
         const float dtx = dv * xv;
-        const float* Bt = sBf + (size_t)t * SP;
-        const float* Ct = sCf + (size_t)t * SP;
+        const float* Bt = sBf + (size_t)j * SP;
+        const float* Ct = sCf + (size_t)j * SP;
         float dA[SP], hp[SP];
         const uint32_t col = tmem + (uint32_t)(j * 2 * SP);
         tmem_load_nowait<SP>(col + SP, dA);
@@ -658,7 +685,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
         } else if (k > 0) {
 #pragma unroll
           for (int q = 0; q < SP / 4; ++q) {
-            const float4 c4 = ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid];
+            const float4 c4 = __ldcg(&ckpt[((size_t)(k - 1) * (SP / 4) + q) * kBwdThreads + tid]);
             hp[4 * q] = c4.x; hp[4 * q + 1] = c4.y; hp[4 * q + 2] = c4.z; hp[4 * q + 3] = c4.w;
           }
         } else {
@@ -814,11 +841,6 @@ __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cas
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 shfl2(float2 v, int m) {
   return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
-}
-__device__ __forceinline__ uint32_t smid() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
-  return r;
 }
 
 template <bool CLAMP>
@@ -1354,12 +1376,10 @@ static int bwd_K(int SP) { return std::min(32, 256 / SP); }
 
 static bool plan_bwd(int64_t nseq, int L, int D, int S, BwdPlan* pl) {
   const int SP = pad_state(S);
-  if (SP == 0 || SP > 16 || nseq <= 0 || L <= 0 || D <= 0) return false;
+  if (SP == 0 || nseq <= 0 || L <= 0 || D <= 0) return false;
   pl->SP = SP;
   pl->K = bwd_K(SP);
   pl->nck = (L + pl->K - 1) / pl->K;
-  // checkpoints: (nck-1) * SP * 128 floats must fit 128 KiB
-  if ((int64_t)(pl->nck - 1) * SP * 128 * 4 > 128 * 1024) return false;
   pl->groups = (D + 127) / 128;
   const int nsm = num_sms();
   // choose the channel split that minimises waves x work per CTA; keep the
@@ -1389,17 +1409,20 @@ static bool plan_bwd(int64_t nseq, int L, int D, int S, BwdPlan* pl) {
   pl->off_p2a = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D * S);
   pl->off_p2d = off;   off = align256(off + sizeof(float) * (size_t)pl->nblk * D);
   pl->off_dbc = off;   off = align256(off + sizeof(float) * (size_t)pl->nsplit * nseq * L * 2 * SP);
-  // checkpoint slots of the packed bf16 kernel (d_state 9..16), one per SM
+  // checkpoint slots, one per SM: the packed bf16 kernel (d_state 9..16) or
+  // the generic kernel, whichever needs more
   pl->nck16 = (L + kW16K - 1) / kW16K;
-  pl->slots = SP == 16 ? std::min(nsm, kW16MaxSlots) : 0;
-  pl->off_ck = off;    off = align256(off + sizeof(float) * (size_t)pl->slots * w16_slot_floats(pl->nck16));
+  pl->slots = std::min(nsm, kW16MaxSlots);
+  const size_t per_slot =
+      std::max(SP == 16 ? w16_slot_floats(pl->nck16) : (size_t)0, gen_slot_floats(pl->nck, SP));
+  pl->off_ck = off;    off = align256(off + sizeof(float) * (size_t)pl->slots * per_slot);
   pl->total = off;
   return true;
 }
 
 template <typename T, int SP, bool CLAMP>
 static int launch_bwd_t(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) {
-  const size_t smem = BwdSmem<T, SP>::total(p.L, p.nck);
+  const size_t smem = BwdSmem<T, SP>::total();
   if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
   auto fn = scan_bwd_kernel<T, SP, CLAMP>;
   if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
@@ -1425,12 +1448,17 @@ static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t s
 template <typename T>
 static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
-    if (pl.SP == 16) return clamp ? launch_bwd_bf16<true>(p, pl, st) : launch_bwd_bf16<false>(p, pl, st);
+    // the packed kernel keeps B, C and dB|dC of the whole sequence in shared
+    // memory; longer sequences take the generic kernel
+    if (pl.SP == 16 && W16Smem::total(p.L) <= 227 * 1024)
+      return clamp ? launch_bwd_bf16<true>(p, pl, st) : launch_bwd_bf16<false>(p, pl, st);
   }
   switch (pl.SP) {
     case 4: return clamp ? launch_bwd_t<T, 4, true>(p, pl, st) : launch_bwd_t<T, 4, false>(p, pl, st);
     case 8: return clamp ? launch_bwd_t<T, 8, true>(p, pl, st) : launch_bwd_t<T, 8, false>(p, pl, st);
     case 16: return clamp ? launch_bwd_t<T, 16, true>(p, pl, st) : launch_bwd_t<T, 16, false>(p, pl, st);
+    case 32: return clamp ? launch_bwd_t<T, 32, true>(p, pl, st) : launch_bwd_t<T, 32, false>(p, pl, st);
+    case 64: return clamp ? launch_bwd_t<T, 64, true>(p, pl, st) : launch_bwd_t<T, 64, false>(p, pl, st);
   }
   return HCLSM_ERR_SHAPE;
 }

@@ -78,8 +78,9 @@ int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_log, const 
  *   dA_log      : (d_inner, d_state) f32
  *   dD          : (d_inner,)         f32  (only when D != NULL)
  * `workspace` must hold hclsm_ssm_scan_bwd_workspace_size(...) bytes.
- * Supported: d_state in {4, 8, 16} with L <= 256*256/(d_state*d_state)
- * (L <= 256 at d_state 16).
+ * Supported: d_state <= 64, any L; d_inner * element size a multiple of 16
+ * bytes; x, dt, dy, z 16-byte aligned.  bf16 with 9 <= d_state <= 16 and
+ * L <= ~600 takes the packed fast kernel.
  * ------------------------------------------------------------------------- */
 size_t hclsm_ssm_scan_bwd_workspace_size(int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state);
 int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const void* B, const void* C,

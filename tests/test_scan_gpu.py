@@ -142,3 +142,20 @@ def test_rejects_cpu():
     d = scan_inputs(2, 4, 8, 4)
     with pytest.raises(ValueError):
         ssm_scan_fn(d["x"], d["dt"], d["A_log"], d["B"], d["C"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(3, 16, 64, 32), (2, 40, 32, 64), (2, 300, 64, 16), (1, 700, 64, 16),
+                                   (2, 129, 48, 24), (1, 1030, 32, 8)])
+def test_bwd_any_state_and_length(dtype, shape):
+    """d_state up to 64 and sequences longer than 256 (the reference's
+    Level0Config default d_state is 64, hclsm/config.py:47)."""
+    nseq, L, Dn, S = shape
+    d = scan_inputs(nseq, L, Dn, S, dtype=dtype, seed=21, device="cuda", gated=True)
+    o = _oracle_inputs(d)
+    for clamp in (False, True):
+        grads = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], d["D"], d["z"], clamp=clamp)
+        gr = oscan.scan_bwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o["dy"], o["D"], o["z"], clamp=clamp)
+        for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), grads):
+            tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
+            assert rel_err(_np(got), gr[name]) < tol, (name, clamp, rel_err(_np(got), gr[name]))
