@@ -21,9 +21,14 @@
 
 #include "common.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace hclsm {
 int* device_err_ptr();
 bool set_smem_limit(const void* fn, size_t bytes);
+int slot_core_tc(const void* Q, const void* K, const void* V, void* out, void* attn, int F, int N, int M, int D,
+                 float scale, float clamp, float eps, int attn_f32, cudaStream_t st);
 }  // namespace hclsm
 
 namespace hclsm {
@@ -497,6 +502,16 @@ extern "C" int hclsm_slot_attn_core(const void* Q, const void* K, const void* V,
   if (D % 16 != 0 || D > 512 || N > 64) return HCLSM_ERR_UNSUPPORTED;
   auto al = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
   if (!al(Q) || !al(K) || !al(V) || !al(out)) return HCLSM_ERR_ALIGN;
+  // tcgen05 core for the shapes it covers; HCLSM_SLOT_CORE=mma selects the
+  // mma.sync core (used by the tests to check one against the other)
+  static const bool force_mma = [] {
+    const char* e = std::getenv("HCLSM_SLOT_CORE");
+    return e && std::strcmp(e, "mma") == 0;
+  }();
+  if (!force_mma) {
+    const int rc = slot_core_tc(Q, K, V, out, attn, F, N, M, D, scale, clamp, eps, attn_f32, st);
+    if (rc != HCLSM_ERR_UNSUPPORTED) return rc;
+  }
   switch ((N + 15) / 16) {
     case 1: return launch_core_nm<1>(p, st);
     case 2: return launch_core_nm<2>(p, st);
