@@ -1,5 +1,6 @@
 // Shared device helpers for the hclsm_b200 kernels (sm_100a only).
 #pragma once
+#include <utility>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -130,6 +131,33 @@ __device__ __forceinline__ float4 ld_hint(const float4* p, uint64_t pol) {
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
+}
+
+// Programmatic dependent launch, device side: wait until the previous kernel
+// on the stream has completed and its writes are visible (no-op when the
+// kernel was not launched as a dependent), and let the next kernel begin its
+// launch.  Every global access of a kernel comes after pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch as a programmatic dependent of the previous kernel on the stream
+// (the kernel must execute griddepcontrol.wait before its first read of data
+// that kernel produced).  Returns an HCLSM status.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? HCLSM_OK
+                                                                                       : HCLSM_ERR_LAUNCH;
 }
 
 }  // namespace hclsm

@@ -77,6 +77,8 @@ template <typename T>
 __global__ void gather_kernel(const T* __restrict__ states, const int32_t* __restrict__ idx,
                               const int32_t* __restrict__ counts, const int32_t* __restrict__ meta, T* __restrict__ out,
                               int64_t frame_elems, int B, int pad_k, int64_t max_frames) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t slot = blockIdx.y;
   if (slot >= max_frames) return;
   int64_t src_frame = -1;
@@ -104,6 +106,8 @@ template <typename T>
 __global__ void scatter_kernel(const T* __restrict__ states, const T* __restrict__ upd,
                                const int32_t* __restrict__ pos, const int32_t* __restrict__ counts, T* __restrict__ out,
                                int64_t frame_elems, int Tlen, int pad_k) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t f = blockIdx.y;
   const int32_t k = pos[f];
   const T* src = states + f * frame_elems;
@@ -157,6 +161,8 @@ template <int TP, int HD>
 __global__ void __launch_bounds__(32) mha_bf16_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                       const uint8_t* __restrict__ key_pad,
                                                       __nv_bfloat16* __restrict__ out, int T, int H, float scale) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RS = HD + 8;  // smem row stride (elements), 16-byte aligned and conflict-free
   __shared__ __align__(16) __nv_bfloat16 sq[TP * RS], sk[TP * RS], sv[TP * RS];
   const int lane = threadIdx.x;
@@ -301,6 +307,8 @@ __global__ void mha_f32_kernel(const float* __restrict__ qkv, const uint8_t* __r
 // SwiGLU: u (rows, 2C) fp32 holding [x W1^T | x W3^T] -> silu(a) * b.
 template <typename TO>
 __global__ void swiglu_kernel(const float* __restrict__ u, TO* __restrict__ y, int64_t rows, int C) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = rows * C;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / C;
@@ -353,12 +361,11 @@ extern "C" int hclsm_event_gather(const void* states, const int32_t* idx, const 
   const int64_t n16 = frame_elems * esz / 16;
   dim3 grid((unsigned)std::min<int64_t>((n16 + 255) / 256, 64), (unsigned)max_frames);
   if (dtype == HCLSM_F32)
-    gather_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(states), idx, counts, meta,
-                                               static_cast<float*>(out), frame_elems, B, pad_k, max_frames);
+    return launch_pdl(gather_kernel<float>, grid, 256, 0, st, static_cast<const float*>(states), idx, counts, meta,
+                      static_cast<float*>(out), frame_elems, B, pad_k, max_frames);
   else if (dtype == HCLSM_BF16)
-    gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(states), idx, counts, meta,
-                                                       static_cast<__nv_bfloat16*>(out), frame_elems, B, pad_k,
-                                                       max_frames);
+    return launch_pdl(gather_kernel<__nv_bfloat16>, grid, 256, 0, st, static_cast<const __nv_bfloat16*>(states), idx,
+                      counts, meta, static_cast<__nv_bfloat16*>(out), frame_elems, B, pad_k, max_frames);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -376,12 +383,12 @@ extern "C" int hclsm_event_scatter(const void* states, const void* upd, const in
   const int64_t n16 = frame_elems * esz / 16;
   dim3 grid((unsigned)std::min<int64_t>((n16 + 255) / 256, 64), (unsigned)frames);
   if (dtype == HCLSM_F32)
-    scatter_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(states), static_cast<const float*>(upd),
-                                                pos, counts, static_cast<float*>(out), frame_elems, T, pad_k);
+    return launch_pdl(scatter_kernel<float>, grid, 256, 0, st, static_cast<const float*>(states),
+                      static_cast<const float*>(upd), pos, counts, static_cast<float*>(out), frame_elems, T, pad_k);
   else if (dtype == HCLSM_BF16)
-    scatter_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(states),
-                                                        static_cast<const __nv_bfloat16*>(upd), pos, counts,
-                                                        static_cast<__nv_bfloat16*>(out), frame_elems, T, pad_k);
+    return launch_pdl(scatter_kernel<__nv_bfloat16>, grid, 256, 0, st, static_cast<const __nv_bfloat16*>(states),
+                      static_cast<const __nv_bfloat16*>(upd), pos, counts, static_cast<__nv_bfloat16*>(out),
+                      frame_elems, T, pad_k);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -390,8 +397,8 @@ extern "C" int hclsm_event_scatter(const void* states, const void* upd, const in
 template <int TP, int HD>
 static void launch_mha(const void* qkv, const uint8_t* kp, void* out, int frames, int T, int H, float scale,
                        cudaStream_t st) {
-  mha_bf16_kernel<TP, HD><<<frames * H, 32, 0, st>>>(static_cast<const __nv_bfloat16*>(qkv), kp,
-                                                     static_cast<__nv_bfloat16*>(out), T, H, scale);
+  (void)launch_pdl(mha_bf16_kernel<TP, HD>, frames * H, 32, 0, st, static_cast<const __nv_bfloat16*>(qkv), kp,
+                   static_cast<__nv_bfloat16*>(out), T, H, scale);
 }
 template <int TP>
 static int launch_mha_tp(const void* qkv, const uint8_t* kp, void* out, int frames, int T, int H, int HD,
@@ -437,9 +444,10 @@ extern "C" int hclsm_swiglu(const float* u, void* y, int64_t rows, int32_t C, in
   if (rows == 0) return HCLSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (out_dtype == HCLSM_BF16)
-    swiglu_kernel<__nv_bfloat16><<<ew_blocks(rows * C), 256, 0, st>>>(u, static_cast<__nv_bfloat16*>(y), rows, C);
+    return launch_pdl(swiglu_kernel<__nv_bfloat16>, ew_blocks(rows * C), 256, 0, st, u,
+                      static_cast<__nv_bfloat16*>(y), rows, C);
   else if (out_dtype == HCLSM_F32)
-    swiglu_kernel<float><<<ew_blocks(rows * C), 256, 0, st>>>(u, static_cast<float*>(y), rows, C);
+    return launch_pdl(swiglu_kernel<float>, ew_blocks(rows * C), 256, 0, st, u, static_cast<float*>(y), rows, C);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;

@@ -323,6 +323,8 @@ __global__ void __launch_bounds__(kThreads) core_f32_kernel(CoreParams p) {
 template <typename TO>
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                  const float* __restrict__ b, TO* __restrict__ y, int64_t rows, int D, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -357,6 +359,8 @@ __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<floa
 __global__ void gru_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
                            const float* __restrict__ b_ih, const float* __restrict__ b_hh,
                            const float* __restrict__ h, float* __restrict__ h_out, int64_t rows, int H) {
+  pdl_wait();
+  pdl_trigger();
   const int Q = H / 4;
   const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -392,6 +396,8 @@ __global__ void gru_kernel(const float* __restrict__ gi, const float* __restrict
 template <typename TO>
 __global__ void bias_act_kernel(const float* __restrict__ x, const float* __restrict__ b, TO* __restrict__ y,
                                 int64_t rows, int C, int act) {
+  pdl_wait();
+  pdl_trigger();
   const int Q = C / 4;
   const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -420,6 +426,8 @@ __global__ void bias_act_kernel(const float* __restrict__ x, const float* __rest
 __global__ void residual_clamp_kernel(const float* __restrict__ h, const float* __restrict__ m,
                                       const float* __restrict__ b, float* __restrict__ out,
                                       __nv_bfloat16* __restrict__ out_bf16, int64_t rows, int C, float c) {
+  pdl_wait();
+  pdl_trigger();
   const int Q = C / 4;
   const int64_t total = rows * Q;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -534,9 +542,10 @@ extern "C" int hclsm_layernorm(const float* x, const float* w, const float* b, v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   if (out_dtype == HCLSM_BF16)
-    layernorm_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(x, w, b, static_cast<__nv_bfloat16*>(y), rows, D, eps);
+    return launch_pdl(layernorm_kernel<__nv_bfloat16>, blocks, 256, 0, st, x, w, b, static_cast<__nv_bfloat16*>(y),
+                      rows, D, eps);
   else if (out_dtype == HCLSM_F32)
-    layernorm_kernel<float><<<blocks, 256, 0, st>>>(x, w, b, static_cast<float*>(y), rows, D, eps);
+    return launch_pdl(layernorm_kernel<float>, blocks, 256, 0, st, x, w, b, static_cast<float*>(y), rows, D, eps);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -548,9 +557,8 @@ extern "C" int hclsm_gru_cell(const float* gi, const float* gh, const float* b_i
   if (rows < 0 || H <= 0) return HCLSM_ERR_SHAPE;
   if (H % 4) return HCLSM_ERR_UNSUPPORTED;
   if (rows == 0) return HCLSM_OK;
-  gru_kernel<<<ew_blocks(rows * H / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(gi, gh, b_ih, b_hh, h, h_out,
-                                                                                 rows, H);
-  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  return launch_pdl(gru_kernel, ew_blocks(rows * H / 4), 256, 0, static_cast<cudaStream_t>(stream), gi, gh, b_ih, b_hh,
+                    h, h_out, rows, H);
 }
 
 extern "C" int hclsm_bias_act(const float* x, const float* b, void* y, int64_t rows, int32_t C, int32_t act,
@@ -561,10 +569,11 @@ extern "C" int hclsm_bias_act(const float* x, const float* b, void* y, int64_t r
   if (rows == 0) return HCLSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (out_dtype == HCLSM_BF16)
-    bias_act_kernel<__nv_bfloat16><<<ew_blocks(rows * C / 4), 256, 0, st>>>(x, b, static_cast<__nv_bfloat16*>(y), rows,
-                                                                        C, act);
+    return launch_pdl(bias_act_kernel<__nv_bfloat16>, ew_blocks(rows * C / 4), 256, 0, st, x, b,
+                      static_cast<__nv_bfloat16*>(y), rows, C, act);
   else if (out_dtype == HCLSM_F32)
-    bias_act_kernel<float><<<ew_blocks(rows * C / 4), 256, 0, st>>>(x, b, static_cast<float*>(y), rows, C, act);
+    return launch_pdl(bias_act_kernel<float>, ew_blocks(rows * C / 4), 256, 0, st, x, b, static_cast<float*>(y), rows,
+                      C, act);
   else
     return HCLSM_ERR_DTYPE;
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -576,7 +585,6 @@ extern "C" int hclsm_residual_clamp(const float* h, const float* m, const float*
   if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
   if (C % 4) return HCLSM_ERR_UNSUPPORTED;
   if (rows == 0) return HCLSM_OK;
-  residual_clamp_kernel<<<ew_blocks(rows * C / 4), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      h, m, b, out, static_cast<__nv_bfloat16*>(out_bf16), rows, C, clamp);
-  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  return launch_pdl(residual_clamp_kernel, ew_blocks(rows * C / 4), 256, 0, static_cast<cudaStream_t>(stream), h, m, b,
+                    out, static_cast<__nv_bfloat16*>(out_bf16), rows, C, clamp);
 }

@@ -147,6 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = s_tmem;
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 
@@ -313,8 +315,7 @@ static int launch_tc(const void* Q, const void* K, const void* V, const TcParams
   const size_t smem = TcSmem::total(NP, p.D);
   auto fn = core_tc_kernel<NP, DB>;
   if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
-  fn<<<p.F, kThreads, smem, st>>>(mq, mk, mv, p);
-  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  return launch_pdl(fn, p.F, kThreads, smem, st, mq, mk, mv, p);
 }
 
 }  // namespace slottc

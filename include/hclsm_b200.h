@@ -40,9 +40,6 @@ typedef enum {
 
 typedef enum { HCLSM_F32 = 0, HCLSM_BF16 = 1 } hclsm_dtype;
 
-/* Epilogues of hclsm_gemm_bf16. */
-typedef enum { HCLSM_EPI_NONE = 0, HCLSM_EPI_RELU = 1, HCLSM_EPI_RESID = 2 } hclsm_epilogue;
-
 /* Library version and the per-device error word.  hclsm_device_error
  * synchronises the device, returns the first recorded error code (0 if none)
  * and clears it. */
@@ -123,21 +120,6 @@ int hclsm_bias_act(const float* x, const float* b, void* y, int64_t rows, int32_
                    int32_t out_dtype, void* stream);
 int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* out, void* out_bf16, int64_t rows,
                          int32_t C, float clamp, void* stream);
-
-/* ---------------------------------------------------------------------------
- * bf16 GEMM on tcgen05 with fused epilogue: acc[m, n] = sum_k A[m, k] W[n, k]
- * (A: M x K, W: N x K, both row-major bf16; fp32 accumulation), then
- *   HCLSM_EPI_NONE : v = acc (+ bias)
- *   HCLSM_EPI_RELU : v = max(acc + bias, 0)
- *   HCLSM_EPI_RESID: v = clamp(acc + bias + resid, -clamp, clamp) (clamp <= 0: none)
- * written to out_f32 and/or out_bf16 (M x N).  The weight products (with their
- * bias / ReLU / residual / clamp) of hclsm/objects/dynamic_slots.py:113-130
- * and hclsm/dynamics/level1_event.py:17-54.  N % 128 == 0, K % 64 == 0,
- * 16-byte aligned pointers; any M.
- * ------------------------------------------------------------------------- */
-int hclsm_gemm_bf16(const void* A, const void* W, int32_t M, int32_t N, int32_t K, int32_t epilogue,
-                    const float* bias, const float* resid, float* out_f32, void* out_bf16, float clamp,
-                    void* stream);
 
 /* ---------------------------------------------------------------------------
  * Sparse event attention.  Replaces the gather / scatter of
