@@ -122,7 +122,7 @@ def run_b200(args, rank, world, local_rank):
     import torch.distributed as dist
 
     import hclsm_b200
-    from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, scan_bwd_raw, scan_fwd_raw
+    from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, scan_bwd_raw, scan_fwd_raw, states_bytes
     from hclsm_b200.workloads import scan_inputs
 
     dev = torch.device("cuda", local_rank)
@@ -130,12 +130,14 @@ def run_b200(args, rank, world, local_rank):
     nseq = args.seqs
     d = scan_inputs(nseq, L, DI, DS, dtype=torch.bfloat16, seed=1000 + rank, device=dev)
     ws = torch.empty(bwd_workspace_bytes(nseq, L, DI, DS), dtype=torch.uint8, device=dev)
+    # the forward keeps h every 10 steps; the backward starts from those snapshots
+    st = torch.empty(states_bytes(nseq, L, DI, DS, torch.bfloat16), dtype=torch.uint8, device=dev)
     y = torch.empty_like(d["x"])
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y)
-        return scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws)
+        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y, states=st)
+        return scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws, states=st)
 
     for _ in range(args.warmup):
         g = step()
@@ -152,9 +154,9 @@ def run_b200(args, rank, world, local_rank):
         dist.barrier()
     ev[0].record(stream)
     for i in range(args.steps):
-        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y)
+        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y, states=st)
         ev[2 * i + 1].record(stream)
-        g = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws)
+        g = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws, states=st)
         ev[2 * i + 2].record(stream)
         del g
     torch.cuda.synchronize(dev)
@@ -171,7 +173,7 @@ def run_b200(args, rank, world, local_rank):
     err = hclsm_b200.device_error()
     if err:
         raise RuntimeError(f"device error {err}")
-    del d, ws, y
+    del d, ws, y, st
     torch.cuda.empty_cache()
     e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)
     return dict(ms_per_step=total_ms / args.steps, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk, e2e=e2e)

@@ -38,6 +38,10 @@ SIGNATURES = {
     "hclsm_ssm_scan_fwd": (ctypes.c_int, [_vp] * 8 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "hclsm_ssm_scan_bwd_workspace_size": (_sz, [_i64, _i32, _i32, _i32]),
     "hclsm_ssm_scan_bwd": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "hclsm_ssm_scan_states_size": (_sz, [_i64, _i32, _i32, _i32, _i32]),
+    "hclsm_ssm_scan_fwd_states": (ctypes.c_int, [_vp] * 8 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
+    "hclsm_ssm_scan_bwd_states": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp,
+                                                              _sz, _vp]),
     "hclsm_slot_attn_core": (ctypes.c_int, [_vp] * 5 + [_i32] * 4 + [ctypes.c_float] * 3 + [_i32, _i32, _vp]),
     "hclsm_layernorm": (ctypes.c_int, [_vp] * 4 + [_i64, _i32, ctypes.c_float, _i32, _vp]),
     "hclsm_gru_cell": (ctypes.c_int, [_vp] * 6 + [_i64, _i32, _vp]),

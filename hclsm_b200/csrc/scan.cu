@@ -52,7 +52,14 @@ struct FwdParams {
   void* y;
   int64_t nseq;
   int L, D, S;
+  // optional (bf16 pair kernel, d_state 9..16): h after every kStateEvery steps,
+  // (nseq, nsnap, D, 16) fp32, nsnap = ceil(L / kStateEvery) - 1
+  float* states;
 };
+
+// steps between the state snapshots the forward keeps for the backward (the
+// packed backward kernel's chunk length)
+constexpr int kStateEvery = 10;
 
 template <typename T, int SP, int CPT, bool CLAMP>
 __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdParams p) {
@@ -218,6 +225,11 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
   const int64_t wD = D / 2;  // 32-bit words per row
   const int64_t col = d0 / 2;
 
+  // state snapshots: this thread's two channels, 64 contiguous bytes each
+  const int nsnap = (L + kStateEvery - 1) / kStateEvery - 1;
+  float* snap = (p.states && act) ? p.states + ((size_t)b * nsnap * D + d0) * 16 : nullptr;
+  int snap_t = kStateEvery;  // step count after which the next snapshot is taken
+
   uint32_t cx[kFwdBlk], cd[kFwdBlk], cz[kFwdBlk];
   auto load_blk = [&](int t0, uint32_t (&ox)[kFwdBlk], uint32_t (&od)[kFwdBlk], uint32_t (&oz)[kFwdBlk]) {
 #pragma unroll
@@ -272,6 +284,19 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
             acc.y *= zv.y * sigmoid(zv.y);
           }
           if (act) __stcs(y + (row0 + t0 + tt) * wD + col, f2_to_bf2(acc.x, acc.y));
+          if constexpr (SP == 16) {
+            if (t0 + tt + 1 == snap_t) {
+              if (snap_t < L && snap) {
+                float4* o = reinterpret_cast<float4*>(snap + (size_t)(snap_t / kStateEvery - 1) * D * 16);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  __stcs(o + q, make_float4(h[4 * q].x, h[4 * q + 1].x, h[4 * q + 2].x, h[4 * q + 3].x));
+                  __stcs(o + 4 + q, make_float4(h[4 * q].y, h[4 * q + 1].y, h[4 * q + 2].y, h[4 * q + 3].y));
+                }
+              }
+              snap_t += kStateEvery;
+            }
+          }
         }
       }
 #pragma unroll
@@ -319,6 +344,7 @@ struct BwdParams {
   int nsplit;
   float* ckpt_ws;   // packed bf16 kernel: per-SM checkpoint slots
   int ckpt_slots;
+  const float* states;  // packed bf16 kernel: the forward's snapshots (no forward sweep), or null
   int* err;
 };
 
@@ -816,6 +842,7 @@ __device__ __forceinline__ void tmem_wait_ld_tied(float (&a)[16], float (&b)[8])
 constexpr int kW16Threads = 256;
 constexpr int kW16Ch = 256;   // channels per group
 constexpr int kW16K = 10;     // history steps per chunk
+static_assert(kW16K == kStateEvery, "the forward's snapshots are the packed kernel's chunk boundaries");
 constexpr int kW16Cols = 24;  // TMEM columns per step: 16 x h (f32) + 8 x dA (f16x2)
 constexpr int kW16MaxSlots = 1024;
 
@@ -866,7 +893,9 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     for (int e = tid; e < L * 8; e += kW16Threads) dst[e] = make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
-  const uint32_t slot = smid();
+  // with the forward's snapshots there is no forward sweep and no checkpoint slot
+  const bool saved = p.states != nullptr;
+  const uint32_t slot = saved ? 0u : smid();
   if (slot >= (uint32_t)p.ckpt_slots) {  // uniform over the block
     if (tid == 0) record_error(p.err, HCLSM_ERR_LAUNCH);
     return;
@@ -917,13 +946,13 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 256);
 
-  const int items_per_group = 2 * nck;
+  const int items_per_group = saved ? nck : 2 * nck;
   const int n_items = (g_end - g_begin) * items_per_group;
   auto issue = [&](int it) {
     if (it >= n_items) return;
     const int g = g_begin + it / items_per_group;
     const int r = it % items_per_group;
-    const bool rev = r >= nck;
+    const bool rev = saved || r >= nck;
     const int k = rev ? (items_per_group - 1 - r) : r;
     const int t0 = k * K;
     const int n = min(K, L - t0);
@@ -962,7 +991,25 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
 #pragma unroll
     for (int q = 0; q < 8; ++q) o[q] = row[q ^ pq];
   };
-  auto load_ck = [&](int k, float2 (&o)[8]) {  // checkpoint before chunk k (k >= 1)
+  auto load_ck = [&](int k, float2 (&o)[8], int d) {  // checkpoint before chunk k (k >= 1)
+    if (saved) {
+      // the forward's snapshot of channel d, states in natural order: float4 m
+      // holds states 4m..4m+3, which this lane keeps in pair slots
+      // 2 (m ^ (perm >> 2)) and 2 (m ^ (perm >> 2)) + 1
+      if (d >= D) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = f2(0.0f, 0.0f);
+        return;
+      }
+      const float4* c = reinterpret_cast<const float4*>(p.states + (((size_t)b * (nck - 1) + (k - 1)) * D + d) * 16);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float4 v = ld_hint(c + (m ^ (perm >> 2)), stream_pol);
+        o[2 * m] = f2(v.x, v.y);
+        o[2 * m + 1] = f2(v.z, v.w);
+      }
+      return;
+    }
     const float4* c = ckpt + (size_t)(k - 1) * 4 * kW16Threads + tid;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -1000,7 +1047,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     float2 h[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) h[q] = f2(0.0f, 0.0f);
-    for (int k = 0; k < nck; ++k, ++it) {
+    for (int k = 0; k < (saved ? 0 : nck); ++k, ++it) {
       wait_item(it);
       const T* st = tiles + (size_t)(it & 1) * 4 * TILE + tid;
       const int t0 = k * K, n = min(K, L - t0);
@@ -1036,7 +1083,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
     for (int q = 0; q < 8; ++q) { gcar[q] = f2(0.0f, 0.0f); gAcc[q] = f2(0.0f, 0.0f); }
     float dDacc = 0.0f;
     if (nck > 1) {
-      load_ck(nck - 1, hk);
+      load_ck(nck - 1, hk, d);
     } else {
 #pragma unroll
       for (int q = 0; q < 8; ++q) hk[q] = f2(0.0f, 0.0f);
@@ -1052,7 +1099,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       for (int q = 0; q < 8; ++q) hs[q] = hk[q];
       // fetch the previous chunk's checkpoint while this chunk runs
       if (k > 1) {
-        load_ck(k - 1, hnext);
+        load_ck(k - 1, hnext, d);
       } else {
 #pragma unroll
         for (int q = 0; q < 8; ++q) hnext[q] = f2(0.0f, 0.0f);
@@ -1331,6 +1378,7 @@ static int launch_fwd_bf16x2(FwdParams p, cudaStream_t st) {
     q.y = static_cast<T*>(p.y) + off;
     q.B = static_cast<const T*>(p.B) + offs;
     q.C = static_cast<const T*>(p.C) + offs;
+    if (p.states) q.states = p.states + s0 * (int64_t)((p.L + kStateEvery - 1) / kStateEvery - 1) * p.D * 16;
     q.nseq = ns;
     scan_fwd_bf16x2_kernel<SP, CLAMP><<<dim3(gx, (unsigned)ns), kFwdThreads, 0, st>>>(q);
   }
@@ -1453,6 +1501,7 @@ static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStr
     if (pl.SP == 16 && W16Smem::total(p.L) <= 227 * 1024)
       return clamp ? launch_bwd_bf16<true>(p, pl, st) : launch_bwd_bf16<false>(p, pl, st);
   }
+  if (p.states) return HCLSM_ERR_UNSUPPORTED;  // only the packed kernel reads snapshots
   switch (pl.SP) {
     case 4: return clamp ? launch_bwd_t<T, 4, true>(p, pl, st) : launch_bwd_t<T, 4, false>(p, pl, st);
     case 8: return clamp ? launch_bwd_t<T, 8, true>(p, pl, st) : launch_bwd_t<T, 8, false>(p, pl, st);
@@ -1478,7 +1527,7 @@ extern "C" int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_
   if (!x || !dt || !A_log || !B || !C || !y) return HCLSM_ERR_NULL;
   if (nseq < 0 || L < 0 || d_inner < 0 || d_state <= 0 || d_state > 64) return HCLSM_ERR_SHAPE;
   if (nseq == 0 || L == 0 || d_inner == 0) return HCLSM_OK;
-  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state};
+  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, nullptr};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == HCLSM_F32) return launch_fwd<float>(p, clamp != 0, st);
   if (dtype == HCLSM_BF16) return launch_fwd<__nv_bfloat16>(p, clamp != 0, st);
@@ -1492,11 +1541,23 @@ extern "C" size_t hclsm_ssm_scan_bwd_workspace_size(int64_t nseq, int32_t L, int
   return pl.total;
 }
 
-extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const void* B,
-                                  const void* C, const float* D, const void* z, const void* dy, void* dx,
-                                  void* ddt, float* dA_log, void* dB, void* dC, float* dD, void* dz,
-                                  int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype,
-                                  int32_t clamp, void* workspace, size_t workspace_bytes, void* stream) {
+// the forward's state snapshots apply where both the bf16 pair forward and the
+// packed backward run: bf16, 9 <= d_state <= 16, even d_inner, B/C/dB|dC of a
+// sequence within shared memory
+static bool states_supported(int64_t nseq, int L, int D, int S, int dtype) {
+  return dtype == HCLSM_BF16 && nseq > 0 && L > 0 && D > 0 && D % 2 == 0 && pad_state(S) == 16 &&
+         W16Smem::total(L) <= 227 * 1024;
+}
+static size_t states_bytes_for(int64_t nseq, int L, int D) {
+  const int64_t nsnap = (L + kStateEvery - 1) / kStateEvery - 1;
+  return std::max<size_t>(16, sizeof(float) * (size_t)nseq * nsnap * D * 16);
+}
+
+static int scan_bwd_impl(const void* x, const void* dt, const float* A_log, const void* B, const void* C,
+                         const float* D, const void* z, const void* dy, void* dx, void* ddt, float* dA_log,
+                         void* dB, void* dC, float* dD, void* dz, int64_t nseq, int32_t L, int32_t d_inner,
+                         int32_t d_state, int32_t dtype, int32_t clamp, const float* states, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   if (!x || !dt || !A_log || !B || !C || !dy || !dx || !ddt || !dA_log || !dB || !dC) return HCLSM_ERR_NULL;
   if (D && !dD) return HCLSM_ERR_NULL;
   if (z && !dz) return HCLSM_ERR_NULL;
@@ -1528,6 +1589,7 @@ extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_
   p.nck = pl.nck; p.groups = pl.groups; p.groups_per_cta = pl.gpc; p.nsplit = pl.nsplit;
   p.ckpt_ws = reinterpret_cast<float*>(ws + pl.off_ck);
   p.ckpt_slots = pl.slots;
+  p.states = states;
   p.err = device_err_ptr();
   int rc = dtype == HCLSM_F32 ? launch_bwd<float>(p, pl, clamp != 0, st)
                               : launch_bwd<__nv_bfloat16>(p, pl, clamp != 0, st);
@@ -1559,4 +1621,51 @@ extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_
                                                           pl.SP, pl.nsplit);
   }
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+}
+
+extern "C" int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const void* B,
+                                  const void* C, const float* D, const void* z, const void* dy, void* dx,
+                                  void* ddt, float* dA_log, void* dB, void* dC, float* dD, void* dz,
+                                  int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype,
+                                  int32_t clamp, void* workspace, size_t workspace_bytes, void* stream) {
+  return scan_bwd_impl(x, dt, A_log, B, C, D, z, dy, dx, ddt, dA_log, dB, dC, dD, dz, nseq, L, d_inner, d_state,
+                       dtype, clamp, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t hclsm_ssm_scan_states_size(int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state,
+                                             int32_t dtype) {
+  if (!states_supported(nseq, L, d_inner, d_state, dtype)) return 0;
+  return states_bytes_for(nseq, L, d_inner);
+}
+
+extern "C" int hclsm_ssm_scan_fwd_states(const void* x, const void* dt, const float* A_log, const void* B,
+                                         const void* C, const float* D, const void* z, void* y, int64_t nseq,
+                                         int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype,
+                                         int32_t clamp, float* states, size_t states_bytes, void* stream) {
+  if (!x || !dt || !A_log || !B || !C || !y || !states) return HCLSM_ERR_NULL;
+  if (nseq < 0 || L < 0 || d_inner < 0 || d_state <= 0 || d_state > 64) return HCLSM_ERR_SHAPE;
+  if (nseq == 0 || L == 0 || d_inner == 0) return HCLSM_OK;
+  if (!states_supported(nseq, L, d_inner, d_state, dtype)) return HCLSM_ERR_UNSUPPORTED;
+  if (states_bytes < states_bytes_for(nseq, L, d_inner)) return HCLSM_ERR_WORKSPACE;
+  auto al4 = [](const void* q) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % 4 == 0; };
+  if (!al4(x) || !al4(dt) || !al4(z) || !al4(y) || !aligned16(states)) return HCLSM_ERR_ALIGN;
+  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, states};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return clamp ? launch_fwd_bf16x2<16, true>(p, st) : launch_fwd_bf16x2<16, false>(p, st);
+}
+
+extern "C" int hclsm_ssm_scan_bwd_states(const void* x, const void* dt, const float* A_log, const void* B,
+                                         const void* C, const float* D, const void* z, const void* dy, void* dx,
+                                         void* ddt, float* dA_log, void* dB, void* dC, float* dD, void* dz,
+                                         int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state,
+                                         int32_t dtype, int32_t clamp, const float* states, size_t states_bytes,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!states) return HCLSM_ERR_NULL;
+  if (nseq > 0 && L > 0) {
+    if (!states_supported(nseq, L, d_inner, d_state, dtype)) return HCLSM_ERR_UNSUPPORTED;
+    if (states_bytes < states_bytes_for(nseq, L, d_inner)) return HCLSM_ERR_WORKSPACE;
+    if (!aligned16(states)) return HCLSM_ERR_ALIGN;
+  }
+  return scan_bwd_impl(x, dt, A_log, B, C, D, z, dy, dx, ddt, dA_log, dB, dC, dD, dz, nseq, L, d_inner, d_state,
+                       dtype, clamp, states, workspace, workspace_bytes, stream);
 }

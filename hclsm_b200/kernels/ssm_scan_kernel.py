@@ -58,11 +58,26 @@ def _check_shapes(x, dt, A_log, B, C, D, z):
     return nseq, L, Dn, S
 
 
-def scan_fwd_raw(x, dt, A_log, B, C, D=None, z=None, clamp=False, out=None):
-    """One forward call through the C ABI; tensors must already be prepared."""
+def states_bytes(nseq, L, Dn, S, dtype) -> int:
+    """Bytes of the forward's state snapshots for the backward (0 where that
+    path does not apply: it needs bf16, 9 <= d_state <= 16, even d_inner)."""
+    return int(_lib.load().hclsm_ssm_scan_states_size(nseq, L, Dn, S, _lib.dtype_code(dtype)))
+
+
+def scan_fwd_raw(x, dt, A_log, B, C, D=None, z=None, clamp=False, out=None, states=None):
+    """One forward call through the C ABI; tensors must already be prepared.
+    With ``states`` (a uint8 tensor of ``states_bytes(...)`` bytes) the forward
+    also keeps h every 10 steps for ``scan_bwd_raw(..., states=...)``."""
     nseq, L, Dn, S = x.shape[0], x.shape[1], x.shape[2], B.shape[-1]
     y = out if out is not None else torch.empty_like(x)
     lib = _lib.load()
+    if states is not None:
+        rc = lib.hclsm_ssm_scan_fwd_states(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
+                                           _lib.ptr(D), _lib.ptr(z), _lib.ptr(y), nseq, L, Dn, S,
+                                           _lib.dtype_code(x.dtype), int(bool(clamp)), _lib.ptr(states),
+                                           states.numel() * states.element_size(), _lib.stream_ptr(x.device))
+        _lib.check(rc, "hclsm_ssm_scan_fwd_states")
+        return y
     rc = lib.hclsm_ssm_scan_fwd(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                 _lib.ptr(D), _lib.ptr(z), _lib.ptr(y), nseq, L, Dn, S,
                                 _lib.dtype_code(x.dtype), int(bool(clamp)), _lib.stream_ptr(x.device))
@@ -74,7 +89,7 @@ def bwd_workspace_bytes(nseq, L, Dn, S) -> int:
     return int(_lib.load().hclsm_ssm_scan_bwd_workspace_size(nseq, L, Dn, S))
 
 
-def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=None):
+def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=None, states=None):
     nseq, L, Dn, S = x.shape[0], x.shape[1], x.shape[2], B.shape[-1]
     lib = _lib.load()
     ws_bytes = bwd_workspace_bytes(nseq, L, Dn, S)
@@ -90,6 +105,15 @@ def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=
     dA = torch.empty(Dn, S, dtype=torch.float32, device=x.device)
     dD = torch.empty(Dn, dtype=torch.float32, device=x.device) if D is not None else None
     dz = torch.empty_like(x) if z is not None else None
+    if states is not None:
+        rc = lib.hclsm_ssm_scan_bwd_states(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
+                                           _lib.ptr(D), _lib.ptr(z), _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(ddt),
+                                           _lib.ptr(dA), _lib.ptr(dB), _lib.ptr(dC), _lib.ptr(dD), _lib.ptr(dz),
+                                           nseq, L, Dn, S, _lib.dtype_code(x.dtype), int(bool(clamp)),
+                                           _lib.ptr(states), states.numel() * states.element_size(),
+                                           _lib.ptr(workspace), workspace.numel(), _lib.stream_ptr(x.device))
+        _lib.check(rc, "hclsm_ssm_scan_bwd_states")
+        return dx, ddt, dA, dB, dC, dD, dz
     rc = lib.hclsm_ssm_scan_bwd(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                 _lib.ptr(D), _lib.ptr(z), _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(ddt),
                                 _lib.ptr(dA), _lib.ptr(dB), _lib.ptr(dC), _lib.ptr(dD), _lib.ptr(dz),
@@ -108,8 +132,15 @@ class _SSMScan(torch.autograd.Function):
         xs, dts, Bs, Cs, zs = (_prep(t, io) for t in (x, dt, B, C, z))
         As = _prep(A_log, torch.float32)
         Ds = _prep(D, torch.float32)
-        y = scan_fwd_raw(xs, dts, As, Bs, Cs, Ds, zs, clamp)
-        ctx.save_for_backward(xs, dts, As, Bs, Cs, Ds, zs)
+        # when a gradient will be asked for and the packed path applies, the
+        # forward keeps state snapshots so the backward skips its forward sweep
+        st = None
+        if any(ctx.needs_input_grad[:7]):
+            nb = states_bytes(xs.shape[0], xs.shape[1], xs.shape[2], Bs.shape[-1], xs.dtype)
+            if nb > 0:
+                st = torch.empty(nb, dtype=torch.uint8, device=xs.device)
+        y = scan_fwd_raw(xs, dts, As, Bs, Cs, Ds, zs, clamp, states=st)
+        ctx.save_for_backward(xs, dts, As, Bs, Cs, Ds, zs, st)
         ctx.clamp = clamp
         ctx.in_dtypes = (x.dtype, dt.dtype, A_log.dtype, B.dtype, C.dtype,
                          None if D is None else D.dtype, None if z is None else z.dtype)
@@ -117,9 +148,9 @@ class _SSMScan(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gy):
-        xs, dts, As, Bs, Cs, Ds, zs = ctx.saved_tensors
+        xs, dts, As, Bs, Cs, Ds, zs, st = ctx.saved_tensors
         dy = _prep(gy, xs.dtype)
-        grads = scan_bwd_raw(xs, dts, As, Bs, Cs, dy, Ds, zs, ctx.clamp)
+        grads = scan_bwd_raw(xs, dts, As, Bs, Cs, dy, Ds, zs, ctx.clamp, states=st)
         out = []
         for g, dtp in zip(grads, ctx.in_dtypes):
             out.append(None if g is None or dtp is None else g.to(dtp))

@@ -90,6 +90,30 @@ int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const 
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Scan forward that keeps state snapshots for the backward, and the backward
+ * that uses them.  No counterpart in the reference (its backward,
+ * ssm_scan_kernel.py:321-377, re-runs the whole forward recurrence): the
+ * forward writes h after every 10 steps, (nseq, ceil(L/10) - 1, d_inner, 16)
+ * fp32, and the backward starts each 10-step chunk from those snapshots
+ * instead of sweeping the recurrence a second time.  Results are identical to
+ * hclsm_ssm_scan_fwd / hclsm_ssm_scan_bwd.
+ * hclsm_ssm_scan_states_size returns the snapshot bytes, or 0 where the path
+ * does not apply (it needs bf16, 9 <= d_state <= 16, even d_inner, and the
+ * packed backward's L limit); then call the plain entry points.
+ * x, dt, z, y 4-byte aligned; states 16-byte aligned.
+ * ------------------------------------------------------------------------- */
+size_t hclsm_ssm_scan_states_size(int64_t nseq, int32_t L, int32_t d_inner, int32_t d_state, int32_t dtype);
+int hclsm_ssm_scan_fwd_states(const void* x, const void* dt, const float* A_log, const void* B, const void* C,
+                              const float* D, const void* z, void* y, int64_t nseq, int32_t L, int32_t d_inner,
+                              int32_t d_state, int32_t dtype, int32_t clamp, float* states, size_t states_bytes,
+                              void* stream);
+int hclsm_ssm_scan_bwd_states(const void* x, const void* dt, const float* A_log, const void* B, const void* C,
+                              const float* D, const void* z, const void* dy, void* dx, void* ddt, float* dA_log,
+                              void* dB, void* dC, float* dD, void* dz, int64_t nseq, int32_t L, int32_t d_inner,
+                              int32_t d_state, int32_t dtype, int32_t clamp, const float* states,
+                              size_t states_bytes, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Slot attention core: out = softmax_over_slots(clamp(Q K^T * scale)) V.
  * Replaces hclsm/kernels/slot_attention_kernel.py:324 slot_attention_fn (the
  * arithmetic of naive_slot_attention :265-291 with eps=0, of the Triton path

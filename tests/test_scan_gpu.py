@@ -159,3 +159,38 @@ def test_bwd_any_state_and_length(dtype, shape):
         for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), grads):
             tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
             assert rel_err(_np(got), gr[name]) < tol, (name, clamp, rel_err(_np(got), gr[name]))
+
+
+@pytest.mark.parametrize("shape", [(3, 256, 2048, 16), (2, 10, 256, 16), (2, 11, 256, 12), (3, 7, 128, 9),
+                                   (2, 100, 512, 16), (1, 257, 384, 13)])
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("clamp", [False, True])
+def test_states_path_identical(shape, gated, clamp):
+    """The forward that keeps state snapshots and the backward that starts its
+    chunks from them compute the same arithmetic as the plain pair: every
+    output is bit-identical."""
+    from hclsm_b200.kernels.ssm_scan_kernel import states_bytes
+    nseq, L, Dn, S = shape
+    d = scan_inputs(nseq, L, Dn, S, dtype=torch.bfloat16, seed=5, device="cuda", gated=gated)
+    D, z = d.get("D"), d.get("z")
+    nb = states_bytes(nseq, L, Dn, S, torch.bfloat16)
+    assert nb > 0
+    st = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    y0 = scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], D, z, clamp=clamp)
+    y1 = scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], D, z, clamp=clamp, states=st)
+    assert torch.equal(y0, y1)
+    g0 = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], D, z, clamp=clamp)
+    g1 = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], D, z, clamp=clamp, states=st)
+    for name, a, b in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), g0, g1):
+        if a is not None:
+            assert torch.equal(a, b), name
+
+
+def test_states_size_gates():
+    """Snapshots only where the packed path runs: bf16, 9 <= d_state <= 16, even d_inner."""
+    from hclsm_b200.kernels.ssm_scan_kernel import states_bytes
+    assert states_bytes(4, 64, 256, 16, torch.bfloat16) == 4 * 6 * 256 * 16 * 4
+    assert states_bytes(4, 64, 256, 16, torch.float32) == 0
+    assert states_bytes(4, 64, 256, 8, torch.bfloat16) == 0
+    assert states_bytes(4, 64, 255, 16, torch.bfloat16) == 0
+    assert states_bytes(4, 5, 256, 16, torch.bfloat16) == 16
