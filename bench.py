@@ -33,9 +33,11 @@ FWD_BYTES_PER_SEQ = 3 * L * DI * 2 + 2 * L * DS * 2
 BWD_BYTES_PER_SEQ = 5 * L * DI * 2 + 4 * L * DS * 2
 ALOG_BYTES = DI * DS * 4
 # DRAM bytes per sequence of the backward kernel measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum, 148-sequence config-4 slice;
-# see profiles/scan_config4_slice_ncu.md).
-BWD_TRAFFIC_PER_SEQ = 5.30e6
+# (dram__bytes_read.sum + dram__bytes_write.sum, 148-sequence config-4 slice
+# on the state-snapshot path; see profiles/scan_config4_slice_ncu.md).  Above
+# the algorithmic bytes by the forward's snapshots that the backward reads
+# (3.28 MB per sequence).
+BWD_TRAFFIC_PER_SEQ = 8.33e6
 
 
 def parse():
@@ -401,12 +403,12 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic", "config": config,
                 "hbm_gbs_algorithmic": (fwd_bytes + bwd_bytes) * world / (ms * 1e-3) / 1e9,
-                "roofline": {"bound": "hbm", "kernel": "scan_bwd_kernel (hclsm_ssm_scan_bwd)",
+                "roofline": {"bound": "hbm", "kernel": "scan_bwd_bf16_kernel (hclsm_ssm_scan_bwd_states)",
                              "achieved": bw_bwd, "peak": hbm_peak, "unit": "GB/s", "frac": bw_bwd / hbm_peak,
                              "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                              "traffic": BWD_TRAFFIC_PER_SEQ * args.seqs, "algorithmic_bytes": bwd_bytes,
                              "ms": r["bwd_ms"]},
-                "roofline_fwd": {"kernel": "scan_fwd (hclsm_ssm_scan_fwd)", "achieved": bw_fwd,
+                "roofline_fwd": {"kernel": "scan_fwd_bf16x2_kernel (hclsm_ssm_scan_fwd_states)", "achieved": bw_fwd,
                                  "frac": bw_fwd / hbm_peak, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes},
                 "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
                 "slot_attention": slot, "event_attention": event,
