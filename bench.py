@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU, help="sequences per GPU")
     ap.add_argument("--e2e-seqs", type=int, default=1024, help="sequences per rank in the end-to-end leg")
+    ap.add_argument("--e2e-chunk", type=int, default=128, help="sequences per pipelined copy/compute chunk")
     ap.add_argument("--ref-seqs", type=int, default=16, help="sequences per CPU-baseline step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -193,7 +194,7 @@ def run_e2e(args, rank, world, dev):
     from hclsm_b200.workloads import scan_inputs
 
     n = args.e2e_seqs
-    chunk = min(256, n)
+    chunk = max(1, min(args.e2e_chunk, n))
     host = {k: v.pin_memory() for k, v in scan_inputs(n, L, DI, DS, dtype=torch.bfloat16, seed=77 + rank).items()}
     outs = {k: torch.empty_like(host["x"]).pin_memory() for k in ("y", "dx", "ddt")}
     outs.update({k: torch.empty_like(host["B"]).pin_memory() for k in ("dB", "dC")})
@@ -205,7 +206,12 @@ def run_e2e(args, rank, world, dev):
     comp = torch.cuda.current_stream(dev)
 
     def step():
-        A = host["A_log"].to(dev, non_blocking=True).requires_grad_(True)
+        # every host->device copy goes through the upload stream: the copy
+        # engine serves copies of one direction in submission order across
+        # streams, so a copy issued on the compute stream would queue behind
+        # all uploads already submitted and stall the compute stream
+        with torch.cuda.stream(up):
+            A = host["A_log"].to(dev, non_blocking=True)
         for s0 in range(0, n, chunk):
             s1 = min(n, s0 + chunk)
             with torch.cuda.stream(up):
@@ -213,6 +219,9 @@ def run_e2e(args, rank, world, dev):
                 ready = torch.cuda.Event()
                 ready.record(up)
             comp.wait_event(ready)
+            if s0 == 0:
+                A.record_stream(comp)
+                A.requires_grad_(True)
             for v in dv.values():
                 v.record_stream(comp)
             leaves = [dv[k].requires_grad_(True) for k in ("x", "dt", "B", "C")]
