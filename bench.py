@@ -350,6 +350,47 @@ def run_event(args, rank, world, dev):
             "config": "BASELINE config 3: 8 videos x 64 steps x 32 slots x 384, 6 heads, 3 layers, p=0.1, bf16"}
 
 
+def run_ssm_block(args, rank, world, dev):
+    """SimplifiedSSMBlock forward + backward (hclsm_b200.install's patched
+    forward: LayerNorm, projections, softplus(dt) + clamp + scan + SiLU gate in
+    one kernel, out_proj, residual) under bf16 autocast, on config-1 scan
+    shapes: 256 sequences x T=64, d_model 384 (d_inner 768), d_state 16."""
+    import torch
+    import torch.distributed as dist
+
+    from hclsm_b200.install import _ssm_block_forward
+    from hclsm_b200.workloads import ssm_block_inputs
+
+    blk, x = ssm_block_inputs(seed=30 + rank, device=dev)
+    x.requires_grad_(True)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = _ssm_block_forward(blk, x)
+        y.float().sum().backward()
+
+    for _ in range(args.warmup):
+        step()
+    reps = 20
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    return {"metric": "ssm_block_fwd_bwd_sequences_per_s", "value": x.shape[0] * world / (ms * 1e-3),
+            "unit": "sequences/s", "ms_per_step": ms,
+            "config": "SimplifiedSSMBlock fwd+bwd, 256 sequences x T=64 x d_model 384 (d_inner 768, d_state 16), "
+                      "bf16 autocast, softplus(dt) fused into the scan"}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -387,6 +428,7 @@ def main():
     dev = torch.device("cuda", local_rank)
     slot = None if args.no_extra else run_slot(args, rank, world, dev)
     event = None if args.no_extra else run_event(args, rank, world, dev)
+    block = None if args.no_extra else run_ssm_block(args, rank, world, dev)
     cpu = None
     if rank == 0 and not args.no_cpu:
         v, cores, _ = cpu_reference(args.ref_seqs, 1, 1)
@@ -420,7 +462,7 @@ def main():
                 "roofline_fwd": {"kernel": "scan_fwd_bf16x2_kernel (hclsm_ssm_scan_fwd_states)", "achieved": bw_fwd,
                                  "frac": bw_fwd / hbm_peak, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes},
                 "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
-                "slot_attention": slot, "event_attention": event,
+                "slot_attention": slot, "event_attention": event, "ssm_block": block,
                 "gpu_launches": 5 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -35,6 +35,11 @@
 namespace hclsm {
 namespace scan {
 
+// softplus(x) = log(1 + e^x) with torch.nn.functional.softplus's default
+// threshold (x > 20 returns x).  Applied to dt when the caller passes the raw
+// dt projection (the flag HCLSM_SCAN_DT_SOFTPLUS).
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
@@ -55,6 +60,7 @@ struct FwdParams {
   // optional (bf16 pair kernel, d_state 9..16): h after every kStateEvery steps,
   // (nseq, nsnap, D, 16) fp32, nsnap = ceil(L / kStateEvery) - 1
   float* states;
+  int softplus;  // dt is the raw projection: softplus is applied inside
 };
 
 // steps between the state snapshots the forward keeps for the backward (the
@@ -123,6 +129,7 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_kernel(FwdParams p) {
       float dtx[CPT], yv[CPT];
 #pragma unroll
       for (int c = 0; c < CPT; ++c) {
+        if (p.softplus) dv[c] = softplus_f(dv[c]);
         if (CLAMP) dv[c] = fminf(fmaxf(dv[c], 1e-3f), 1.0f);
         dtx[c] = dv[c] * xv[c];
         yv[c] = 0.0f;
@@ -264,6 +271,10 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
         if (tt < tc) {
           float2 xv = bf2_to_f2(cx[j]);
           float2 dv = bf2_to_f2(cd[j]);
+          if (p.softplus) {
+            dv.x = softplus_f(dv.x);
+            dv.y = softplus_f(dv.y);
+          }
           if (CLAMP) {
             dv.x = fminf(fmaxf(dv.x, 1e-3f), 1.0f);
             dv.y = fminf(fmaxf(dv.y, 1e-3f), 1.0f);
@@ -345,6 +356,7 @@ struct BwdParams {
   float* ckpt_ws;   // packed bf16 kernel: per-SM checkpoint slots
   int ckpt_slots;
   const float* states;  // packed bf16 kernel: the forward's snapshots (no forward sweep), or null
+  int softplus;         // dt is the raw projection: softplus is applied inside
   int* err;
 };
 
@@ -640,6 +652,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
       for (int j = 0; j < n; ++j) {
         float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
         float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
+        if (p.softplus) dv = softplus_f(dv);
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float dtx = dv * xv;
         const float* Bt = sBf + (size_t)j * SP;
@@ -675,6 +688,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
       for (int j = 0; j < n; ++j) {
         float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
         float dv = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
+        if (p.softplus) dv = softplus_f(dv);
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float dtx = dv * xv;
         const float* Bt = sBf + (size_t)j * SP;
@@ -695,10 +709,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) scan_bwd_kernel(BwdParams p) {
         float xv = act ? io<T>::ld(st + (size_t)j * kBwdThreads + tid) : 0.0f;
         const float draw = act ? io<T>::ld(st + ((size_t)K + j) * kBwdThreads + tid) : 0.0f;
         float gy = act ? io<T>::ld(st + ((size_t)2 * K + j) * kBwdThreads + tid) : 0.0f;
+        // dv = clamp(softplus(raw)); mdt = d dv / d raw
         float dv = draw, mdt = 1.0f;
+        if (p.softplus) {
+          dv = softplus_f(draw);
+          mdt = sigmoid(draw);
+        }
         if (CLAMP) {
-          mdt = (draw >= 1e-3f && draw <= 1.0f) ? 1.0f : 0.0f;
-          dv = fminf(fmaxf(draw, 1e-3f), 1.0f);
+          mdt = (dv >= 1e-3f && dv <= 1.0f) ? mdt : 0.0f;
+          dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         }
         const float dtx = dv * xv;
         const float* Bt = sBf + (size_t)j * SP;
@@ -870,7 +889,7 @@ __device__ __forceinline__ float2 shfl2(float2 v, int m) {
   return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-template <bool CLAMP>
+template <bool CLAMP, bool SOFTPLUS>
 __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams p) {
   using T = __nv_bfloat16;
   using Sm = W16Smem;
@@ -1061,6 +1080,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       for (int j = 0; j < n; ++j) {
         const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
         float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        if (SOFTPLUS) dv = softplus_f(dv);
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float2 dtx = f2(dv * xv, dv * xv);
         const float2 dvv2 = f2(dv, dv);
@@ -1109,6 +1129,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       for (int j = 0; j < n; ++j) {
         const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
         float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        if (SOFTPLUS) dv = softplus_f(dv);
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float2 dtx = f2(dv * xv, dv * xv);
         const float2 dvv2 = f2(dv, dv);
@@ -1159,10 +1180,15 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
         const float draw = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
         float gy = act ? __bfloat162float(st[2 * TILE + (size_t)j * kW16Ch]) : 0.0f;
+        // dv = clamp(softplus(raw)); mdt = d dv / d raw
         float dv = draw, mdt = 1.0f;
+        if (SOFTPLUS) {
+          dv = softplus_f(draw);
+          mdt = sigmoid(draw);
+        }
         if (CLAMP) {
-          mdt = (draw >= 1e-3f && draw <= 1.0f) ? 1.0f : 0.0f;
-          dv = fminf(fmaxf(draw, 1e-3f), 1.0f);
+          mdt = (dv >= 1e-3f && dv <= 1.0f) ? mdt : 0.0f;
+          dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         }
         const float dtxs = dv * xv;
         float2 Bt[8], Ct[8];
@@ -1478,7 +1504,7 @@ static int launch_bwd_t(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) 
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
 }
 
-template <bool CLAMP>
+template <bool CLAMP, bool SOFTPLUS>
 static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) {
   const size_t smem = W16Smem::total(p.L);
   if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
@@ -1487,7 +1513,7 @@ static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t s
   q.groups = (p.D + kW16Ch - 1) / kW16Ch;
   // the channel split of the plan counts 128-channel groups; keep its CTA count
   q.groups_per_cta = (q.groups + pl.nsplit - 1) / pl.nsplit;
-  auto fn = scan_bwd_bf16_kernel<CLAMP>;
+  auto fn = scan_bwd_bf16_kernel<CLAMP, SOFTPLUS>;
   if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
   fn<<<dim3((unsigned)p.nseq, pl.nsplit), kW16Threads, smem, st>>>(q);
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -1498,8 +1524,11 @@ static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStr
   if constexpr (sizeof(T) == 2) {
     // the packed kernel keeps B, C and dB|dC of the whole sequence in shared
     // memory; longer sequences take the generic kernel
-    if (pl.SP == 16 && W16Smem::total(p.L) <= 227 * 1024)
-      return clamp ? launch_bwd_bf16<true>(p, pl, st) : launch_bwd_bf16<false>(p, pl, st);
+    if (pl.SP == 16 && W16Smem::total(p.L) <= 227 * 1024) {
+      if (p.softplus)
+        return clamp ? launch_bwd_bf16<true, true>(p, pl, st) : launch_bwd_bf16<false, true>(p, pl, st);
+      return clamp ? launch_bwd_bf16<true, false>(p, pl, st) : launch_bwd_bf16<false, false>(p, pl, st);
+    }
   }
   if (p.states) return HCLSM_ERR_UNSUPPORTED;  // only the packed kernel reads snapshots
   switch (pl.SP) {
@@ -1527,10 +1556,13 @@ extern "C" int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_
   if (!x || !dt || !A_log || !B || !C || !y) return HCLSM_ERR_NULL;
   if (nseq < 0 || L < 0 || d_inner < 0 || d_state <= 0 || d_state > 64) return HCLSM_ERR_SHAPE;
   if (nseq == 0 || L == 0 || d_inner == 0) return HCLSM_OK;
-  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, nullptr};
+  if (clamp & ~(HCLSM_SCAN_CLAMP | HCLSM_SCAN_DT_SOFTPLUS)) return HCLSM_ERR_SHAPE;
+  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, nullptr,
+              (clamp & HCLSM_SCAN_DT_SOFTPLUS) ? 1 : 0};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == HCLSM_F32) return launch_fwd<float>(p, clamp != 0, st);
-  if (dtype == HCLSM_BF16) return launch_fwd<__nv_bfloat16>(p, clamp != 0, st);
+  const bool cl = (clamp & HCLSM_SCAN_CLAMP) != 0;
+  if (dtype == HCLSM_F32) return launch_fwd<float>(p, cl, st);
+  if (dtype == HCLSM_BF16) return launch_fwd<__nv_bfloat16>(p, cl, st);
   return HCLSM_ERR_DTYPE;
 }
 
@@ -1563,6 +1595,7 @@ static int scan_bwd_impl(const void* x, const void* dt, const float* A_log, cons
   if (z && !dz) return HCLSM_ERR_NULL;
   if (nseq < 0 || L < 0 || d_inner <= 0 || d_state <= 0) return HCLSM_ERR_SHAPE;
   if (dtype != HCLSM_F32 && dtype != HCLSM_BF16) return HCLSM_ERR_DTYPE;
+  if (clamp & ~(HCLSM_SCAN_CLAMP | HCLSM_SCAN_DT_SOFTPLUS)) return HCLSM_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (nseq == 0 || L == 0) {
     cudaMemsetAsync(dA_log, 0, sizeof(float) * (size_t)d_inner * d_state, st);
@@ -1590,9 +1623,10 @@ static int scan_bwd_impl(const void* x, const void* dt, const float* A_log, cons
   p.ckpt_ws = reinterpret_cast<float*>(ws + pl.off_ck);
   p.ckpt_slots = pl.slots;
   p.states = states;
+  p.softplus = (clamp & HCLSM_SCAN_DT_SOFTPLUS) ? 1 : 0;
   p.err = device_err_ptr();
-  int rc = dtype == HCLSM_F32 ? launch_bwd<float>(p, pl, clamp != 0, st)
-                              : launch_bwd<__nv_bfloat16>(p, pl, clamp != 0, st);
+  const bool cl = (clamp & HCLSM_SCAN_CLAMP) != 0;
+  int rc = dtype == HCLSM_F32 ? launch_bwd<float>(p, pl, cl, st) : launch_bwd<__nv_bfloat16>(p, pl, cl, st);
   if (rc != HCLSM_OK) return rc;
   // dA_log and dD: deterministic column sums over sequences
   {
@@ -1649,9 +1683,11 @@ extern "C" int hclsm_ssm_scan_fwd_states(const void* x, const void* dt, const fl
   if (states_bytes < states_bytes_for(nseq, L, d_inner)) return HCLSM_ERR_WORKSPACE;
   auto al4 = [](const void* q) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % 4 == 0; };
   if (!al4(x) || !al4(dt) || !al4(z) || !al4(y) || !aligned16(states)) return HCLSM_ERR_ALIGN;
-  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, states};
+  if (clamp & ~(HCLSM_SCAN_CLAMP | HCLSM_SCAN_DT_SOFTPLUS)) return HCLSM_ERR_SHAPE;
+  FwdParams p{x, dt, A_log, B, C, D, z, y, nseq, L, d_inner, d_state, states,
+              (clamp & HCLSM_SCAN_DT_SOFTPLUS) ? 1 : 0};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return clamp ? launch_fwd_bf16x2<16, true>(p, st) : launch_fwd_bf16x2<16, false>(p, st);
+  return (clamp & HCLSM_SCAN_CLAMP) ? launch_fwd_bf16x2<16, true>(p, st) : launch_fwd_bf16x2<16, false>(p, st);
 }
 
 extern "C" int hclsm_ssm_scan_bwd_states(const void* x, const void* dt, const float* A_log, const void* B,

@@ -8,9 +8,10 @@ What is replaced (paths inside RightNow-AI/hclsm):
 * ``hclsm.kernels.ssm_scan_fn`` and ``hclsm.kernels.ssm_scan_kernel.ssm_scan_fn``
   (the package re-exports by value, hclsm/kernels/__init__.py:9-35, so both
   names are patched), likewise ``slot_attention_fn`` and ``sparse_event_attn_fn``;
-* ``SimplifiedSSMBlock.forward`` (hclsm/dynamics/level0_ssm.py:58-107): the
-  inline clamped scan and the SiLU gate run as one differentiable kernel call
-  (clamp=True, z = gate_proj(x));
+* ``SimplifiedSSMBlock.forward`` (hclsm/dynamics/level0_ssm.py:58-107):
+  softplus(dt_proj(z)) with its clamp, the inline clamped scan and the SiLU
+  gate run as one differentiable kernel call (clamp=True, dt_softplus=True,
+  z = gate_proj(x));
 * ``DynamicSlotAttention._iteration_step`` (hclsm/objects/dynamic_slots.py:98-131);
 * ``HierarchyManager.gather_events`` / ``scatter_events``
   (hclsm/dynamics/hierarchy_manager.py:42-118);
@@ -25,7 +26,6 @@ tensors are not accepted by the replaced functions (no CPU fallback).
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 _ORIG = {}
 
@@ -55,17 +55,17 @@ def uninstall():
 
 
 def _ssm_block_forward(self, x):
-    """SimplifiedSSMBlock.forward with the scan and gate fused (level0_ssm.py:58-107)."""
+    """SimplifiedSSMBlock.forward with softplus(dt), its clamp, the scan and
+    the gate in one kernel (level0_ssm.py:58-107)."""
     from .kernels import ssm_scan
 
     residual = x
     x = self.norm(x)
     z = self.in_proj(x)
     gate_pre = self.gate_proj(x)
-    dt = F.softplus(self.dt_proj(z)).clamp(min=1e-3, max=1.0)
     B_param = self.B_proj(z)
     C_param = self.C_proj(z)
-    y = ssm_scan(z, dt, self.A_log, B_param, C_param, clamp=True, z=gate_pre)
+    y = ssm_scan(z, self.dt_proj(z), self.A_log, B_param, C_param, clamp=True, z=gate_pre, dt_softplus=True)
     y = self.out_proj(y.to(residual.dtype))
     return residual + y
 

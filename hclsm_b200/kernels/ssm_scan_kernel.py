@@ -64,23 +64,31 @@ def states_bytes(nseq, L, Dn, S, dtype) -> int:
     return int(_lib.load().hclsm_ssm_scan_states_size(nseq, L, Dn, S, _lib.dtype_code(dtype)))
 
 
-def scan_fwd_raw(x, dt, A_log, B, C, D=None, z=None, clamp=False, out=None, states=None):
+def _flags(clamp, dt_softplus):
+    """The scan entry points' flags argument: bit 0 clamped arithmetic, bit 1
+    softplus applied to the raw dt inside the kernel."""
+    return int(bool(clamp)) | (2 if dt_softplus else 0)
+
+
+def scan_fwd_raw(x, dt, A_log, B, C, D=None, z=None, clamp=False, out=None, states=None, dt_softplus=False):
     """One forward call through the C ABI; tensors must already be prepared.
     With ``states`` (a uint8 tensor of ``states_bytes(...)`` bytes) the forward
-    also keeps h every 10 steps for ``scan_bwd_raw(..., states=...)``."""
+    also keeps h every 10 steps for ``scan_bwd_raw(..., states=...)``.  With
+    ``dt_softplus`` dt is the raw projection and softplus is applied inside."""
     nseq, L, Dn, S = x.shape[0], x.shape[1], x.shape[2], B.shape[-1]
+    flags = _flags(clamp, dt_softplus)
     y = out if out is not None else torch.empty_like(x)
     lib = _lib.load()
     if states is not None:
         rc = lib.hclsm_ssm_scan_fwd_states(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                            _lib.ptr(D), _lib.ptr(z), _lib.ptr(y), nseq, L, Dn, S,
-                                           _lib.dtype_code(x.dtype), int(bool(clamp)), _lib.ptr(states),
+                                           _lib.dtype_code(x.dtype), flags, _lib.ptr(states),
                                            states.numel() * states.element_size(), _lib.stream_ptr(x.device))
         _lib.check(rc, "hclsm_ssm_scan_fwd_states")
         return y
     rc = lib.hclsm_ssm_scan_fwd(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                 _lib.ptr(D), _lib.ptr(z), _lib.ptr(y), nseq, L, Dn, S,
-                                _lib.dtype_code(x.dtype), int(bool(clamp)), _lib.stream_ptr(x.device))
+                                _lib.dtype_code(x.dtype), flags, _lib.stream_ptr(x.device))
     _lib.check(rc, "hclsm_ssm_scan_fwd")
     return y
 
@@ -89,8 +97,12 @@ def bwd_workspace_bytes(nseq, L, Dn, S) -> int:
     return int(_lib.load().hclsm_ssm_scan_bwd_workspace_size(nseq, L, Dn, S))
 
 
-def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=None, states=None):
+def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=None, states=None,
+                 dt_softplus=False):
+    """Gradients (dx, ddt, dA_log, dB, dC, dD, dz); with ``dt_softplus`` ddt is
+    the gradient of the raw dt."""
     nseq, L, Dn, S = x.shape[0], x.shape[1], x.shape[2], B.shape[-1]
+    flags = _flags(clamp, dt_softplus)
     lib = _lib.load()
     ws_bytes = bwd_workspace_bytes(nseq, L, Dn, S)
     if ws_bytes == 0 and nseq * L > 0:
@@ -109,7 +121,7 @@ def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=
         rc = lib.hclsm_ssm_scan_bwd_states(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                            _lib.ptr(D), _lib.ptr(z), _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(ddt),
                                            _lib.ptr(dA), _lib.ptr(dB), _lib.ptr(dC), _lib.ptr(dD), _lib.ptr(dz),
-                                           nseq, L, Dn, S, _lib.dtype_code(x.dtype), int(bool(clamp)),
+                                           nseq, L, Dn, S, _lib.dtype_code(x.dtype), flags,
                                            _lib.ptr(states), states.numel() * states.element_size(),
                                            _lib.ptr(workspace), workspace.numel(), _lib.stream_ptr(x.device))
         _lib.check(rc, "hclsm_ssm_scan_bwd_states")
@@ -117,7 +129,7 @@ def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=
     rc = lib.hclsm_ssm_scan_bwd(_lib.ptr(x), _lib.ptr(dt), _lib.ptr(A_log), _lib.ptr(B), _lib.ptr(C),
                                 _lib.ptr(D), _lib.ptr(z), _lib.ptr(dy), _lib.ptr(dx), _lib.ptr(ddt),
                                 _lib.ptr(dA), _lib.ptr(dB), _lib.ptr(dC), _lib.ptr(dD), _lib.ptr(dz),
-                                nseq, L, Dn, S, _lib.dtype_code(x.dtype), int(bool(clamp)),
+                                nseq, L, Dn, S, _lib.dtype_code(x.dtype), flags,
                                 _lib.ptr(workspace), workspace.numel(), _lib.stream_ptr(x.device))
     _lib.check(rc, "hclsm_ssm_scan_bwd")
     return dx, ddt, dA, dB, dC, dD, dz
@@ -125,7 +137,7 @@ def scan_bwd_raw(x, dt, A_log, B, C, dy, D=None, z=None, clamp=False, workspace=
 
 class _SSMScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, dt, A_log, B, C, D, z, clamp):
+    def forward(ctx, x, dt, A_log, B, C, D, z, clamp, dt_softplus):
         _lib.require_cuda(x, dt, A_log, B, C, D, z)
         _check_shapes(x, dt, A_log, B, C, D, z)
         io = _io_dtype(x, dt, B, C, z)
@@ -139,9 +151,10 @@ class _SSMScan(torch.autograd.Function):
             nb = states_bytes(xs.shape[0], xs.shape[1], xs.shape[2], Bs.shape[-1], xs.dtype)
             if nb > 0:
                 st = torch.empty(nb, dtype=torch.uint8, device=xs.device)
-        y = scan_fwd_raw(xs, dts, As, Bs, Cs, Ds, zs, clamp, states=st)
+        y = scan_fwd_raw(xs, dts, As, Bs, Cs, Ds, zs, clamp, states=st, dt_softplus=dt_softplus)
         ctx.save_for_backward(xs, dts, As, Bs, Cs, Ds, zs, st)
         ctx.clamp = clamp
+        ctx.dt_softplus = dt_softplus
         ctx.in_dtypes = (x.dtype, dt.dtype, A_log.dtype, B.dtype, C.dtype,
                          None if D is None else D.dtype, None if z is None else z.dtype)
         return y.to(x.dtype)
@@ -150,19 +163,21 @@ class _SSMScan(torch.autograd.Function):
     def backward(ctx, gy):
         xs, dts, As, Bs, Cs, Ds, zs, st = ctx.saved_tensors
         dy = _prep(gy, xs.dtype)
-        grads = scan_bwd_raw(xs, dts, As, Bs, Cs, dy, Ds, zs, ctx.clamp, states=st)
+        grads = scan_bwd_raw(xs, dts, As, Bs, Cs, dy, Ds, zs, ctx.clamp, states=st, dt_softplus=ctx.dt_softplus)
         out = []
         for g, dtp in zip(grads, ctx.in_dtypes):
             out.append(None if g is None or dtp is None else g.to(dtp))
-        return (*out, None)
+        return (*out, None, None)
 
 
-def ssm_scan(x, dt, A_log, B, C, *, clamp=False, D=None, z=None):
-    """Selective scan on sm_100a; differentiable in every tensor argument."""
-    return _SSMScan.apply(x, dt, A_log, B, C, D, z, bool(clamp))
+def ssm_scan(x, dt, A_log, B, C, *, clamp=False, D=None, z=None, dt_softplus=False):
+    """Selective scan on sm_100a; differentiable in every tensor argument.
+    ``dt_softplus``: dt is the raw projection, softplus(dt) is taken inside the
+    kernel (and its gradient is the raw dt's)."""
+    return _SSMScan.apply(x, dt, A_log, B, C, D, z, bool(clamp), bool(dt_softplus))
 
 
-def ssm_scan_fn(x, dt, A_log, B, C, backend: str = "auto", *, clamp=None, D=None, z=None):
+def ssm_scan_fn(x, dt, A_log, B, C, backend: str = "auto", *, clamp=None, D=None, z=None, dt_softplus=False):
     """Drop-in for ``hclsm.kernels.ssm_scan_fn`` (ssm_scan_kernel.py:394).
 
     ``backend`` accepts the reference's names ("auto", "triton", "parallel",
@@ -174,4 +189,4 @@ def ssm_scan_fn(x, dt, A_log, B, C, backend: str = "auto", *, clamp=None, D=None
         raise ValueError(f"unknown backend {backend!r}")
     if clamp is None:
         clamp = backend == "sequential"
-    return ssm_scan(x, dt, A_log, B, C, clamp=clamp, D=D, z=z)
+    return ssm_scan(x, dt, A_log, B, C, clamp=clamp, D=D, z=z, dt_softplus=dt_softplus)

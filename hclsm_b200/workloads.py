@@ -115,3 +115,34 @@ def event_inputs(B=8, T=64, N=32, D=384, heads=6, layers=3, p=0.1, seed=0, devic
             w[q + nm + ".weight"] = torch.ones(D, device=device)
             w[q + nm + ".bias"] = torch.zeros(D, device=device)
     return {"states": states, "mask": mask, "weights": w, "heads": heads, "layers": layers}
+
+
+class SSMBlockModule(torch.nn.Module):
+    """Parameters of SimplifiedSSMBlock (hclsm/dynamics/level0_ssm.py:36-56)
+    under the same attribute names, so that hclsm_b200.install's patched
+    forward runs on it without the reference package: in_proj / gate_proj
+    (d_model -> 2 d_model, no bias), dt_proj (with bias), B_proj / C_proj (no
+    bias), A_log ~ -U(0, 0.5), out_proj, LayerNorm; nn.Linear's default init."""
+
+    def __init__(self, d_model: int, d_state: int, expand: int = 2):
+        super().__init__()
+        di = d_model * expand
+        self.d_model, self.d_state = d_model, d_state
+        self.in_proj = torch.nn.Linear(d_model, di, bias=False)
+        self.gate_proj = torch.nn.Linear(d_model, di, bias=False)
+        self.dt_proj = torch.nn.Linear(di, di, bias=True)
+        self.B_proj = torch.nn.Linear(di, d_state, bias=False)
+        self.C_proj = torch.nn.Linear(di, d_state, bias=False)
+        self.A_log = torch.nn.Parameter(-torch.rand(di, d_state) * 0.5)
+        self.out_proj = torch.nn.Linear(di, d_model, bias=False)
+        self.norm = torch.nn.LayerNorm(d_model)
+
+
+def ssm_block_inputs(nseq=256, T=64, d_model=384, d_state=16, seed=0, device="cpu"):
+    """A SimplifiedSSMBlock-shaped module and its input (nseq, T, d_model) ~
+    N(0, 1); d_model 384 gives d_inner 768, BASELINE config 1's scan shape."""
+    torch.manual_seed(seed)
+    blk = SSMBlockModule(d_model, d_state).to(device)
+    g = torch.Generator(device="cpu").manual_seed(seed + 1)
+    x = torch.randn(nseq, T, d_model, generator=g).to(device)
+    return blk, x

@@ -40,6 +40,10 @@ typedef enum {
 
 typedef enum { HCLSM_F32 = 0, HCLSM_BF16 = 1 } hclsm_dtype;
 
+/* Flags of the scan entry points' `clamp` argument (0 and 1 keep their
+ * meaning: the unclamped and the clamped arithmetic). */
+typedef enum { HCLSM_SCAN_CLAMP = 1, HCLSM_SCAN_DT_SOFTPLUS = 2 } hclsm_scan_flags;
+
 /* Library version and the per-device error word.  hclsm_device_error
  * synchronises the device, returns the first recorded error code (0 if none)
  * and clears it. */
@@ -61,6 +65,11 @@ int hclsm_selftest_wait_timeout(uint32_t polls, int* status_dev, void* stream);
  *   A_log       : (d_inner, d_state)   f32
  *   D           : (d_inner,)           f32, optional (NULL)
  *   z           : optional (NULL); when given y = (scan + D*x) * silu(z)
+ *   clamp       : flags, HCLSM_SCAN_CLAMP for the clamped arithmetic and/or
+ *                 HCLSM_SCAN_DT_SOFTPLUS when dt is the raw projection and
+ *                 softplus(dt) (torch's threshold 20) is applied inside, as
+ *                 SimplifiedSSMBlock does before its scan (level0_ssm.py:76);
+ *                 the backward then returns the gradient of the raw dt
  * d_state <= 64.  State and arithmetic are fp32 for both dtypes.
  * ------------------------------------------------------------------------- */
 int hclsm_ssm_scan_fwd(const void* x, const void* dt, const float* A_log, const void* B,

@@ -194,3 +194,39 @@ def test_states_size_gates():
     assert states_bytes(4, 64, 256, 8, torch.bfloat16) == 0
     assert states_bytes(4, 64, 255, 16, torch.bfloat16) == 0
     assert states_bytes(4, 5, 256, 16, torch.bfloat16) == 16
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(3, 17, 40, 16), (2, 64, 256, 16), (2, 33, 136, 8), (1, 256, 2048, 16)])
+@pytest.mark.parametrize("clamp", [False, True])
+def test_dt_softplus_vs_oracle(dtype, shape, clamp):
+    """dt given as the raw projection (SimplifiedSSMBlock's dt_proj(z),
+    level0_ssm.py:76): the kernel takes softplus inside; the oracle gets
+    softplus(raw) and the raw gradient follows by the chain rule."""
+    nseq, L, Dn, S = shape
+    d = scan_inputs(nseq, L, Dn, S, dtype=dtype, seed=21, device="cuda")
+    g = torch.Generator(device="cpu").manual_seed(5)
+    raw = (torch.randn(nseq, L, Dn, generator=g) * 2.0 - 1.5).to(dtype).cuda()
+    y = scan_fwd_raw(d["x"], raw, d["A_log"], d["B"], d["C"], clamp=clamp, dt_softplus=True)
+    grads = scan_bwd_raw(d["x"], raw, d["A_log"], d["B"], d["C"], d["dy"], clamp=clamp, dt_softplus=True)
+    o = _oracle_inputs(d)
+    raw64 = raw.double().cpu()
+    dt_eff = torch.nn.functional.softplus(raw64).float().numpy()
+    yr = oscan.scan_fwd(o["x"], dt_eff, o["A_log"], o["B"], o["C"], clamp=clamp)
+    assert rel_err(_np(y), yr) < TOL[dtype]
+    gr = oscan.scan_bwd(o["x"], dt_eff, o["A_log"], o["B"], o["C"], o["dy"], clamp=clamp)
+    gr["ddt"] = gr["ddt"] * torch.sigmoid(raw64).numpy()
+    tol = TOL[dtype] if dtype == torch.bfloat16 else 2e-5
+    for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC"), grads):
+        assert rel_err(_np(got), gr[name]) < tol, (name, rel_err(_np(got), gr[name]))
+    if dtype == torch.bfloat16 and S == 16 and Dn % 2 == 0:
+        # the state-snapshot pair gives the same bits
+        from hclsm_b200.kernels.ssm_scan_kernel import states_bytes
+        st = torch.empty(states_bytes(nseq, L, Dn, S, dtype), dtype=torch.uint8, device="cuda")
+        y1 = scan_fwd_raw(d["x"], raw, d["A_log"], d["B"], d["C"], clamp=clamp, dt_softplus=True, states=st)
+        g1 = scan_bwd_raw(d["x"], raw, d["A_log"], d["B"], d["C"], d["dy"], clamp=clamp, dt_softplus=True,
+                          states=st)
+        assert torch.equal(y, y1)
+        for a, b in zip(grads, g1):
+            if a is not None:
+                assert torch.equal(a, b)
