@@ -17,6 +17,7 @@
 """
 from __future__ import annotations
 
+from collections import OrderedDict
 from dataclasses import dataclass, field
 
 import torch
@@ -56,11 +57,13 @@ def event_compact(event_mask):
     return idx, pos, counts, meta
 
 
-def event_gather(states, idx, counts, meta, n_frames, pad_k=0):
+def event_gather(states, idx, counts, meta, n_frames, pad_k=0, out=None):
     """(n_frames, N, D) compacted frames (pad_k=0) or the padded (B*pad_k, N, D)
-    layout with zero pad frames."""
+    layout with zero pad frames; written into ``out`` (contiguous, at least
+    n_frames frames) when given."""
     B, T, N, D = states.shape
-    out = torch.empty(n_frames, N, D, dtype=states.dtype, device=states.device)
+    if out is None:
+        out = torch.empty(n_frames, N, D, dtype=states.dtype, device=states.device)
     if n_frames == 0:
         return out
     rc = _lib.load().hclsm_event_gather(_lib.ptr(states), _lib.ptr(idx), _lib.ptr(counts), _lib.ptr(meta),
@@ -106,6 +109,12 @@ class EventTransformer:
     norm_b: torch.Tensor
     layers: list = field(default_factory=list)
     dtype: torch.dtype = torch.bfloat16
+    # CUDA graphs of the whole stack, one per (frame bucket, N, d_slot, key
+    # mask, input dtype, device); every op is per row or per frame, so rows of a
+    # bucket past the real frame count do not touch the real rows
+    _graphs: OrderedDict = field(default_factory=OrderedDict, repr=False, compare=False)
+    _pool: object = field(default=None, repr=False, compare=False)
+    max_graphs: int = 32
 
     @classmethod
     def from_state(cls, sd: dict, n_heads: int, device, dtype=torch.bfloat16):
@@ -139,7 +148,52 @@ class EventTransformer:
 
     def __call__(self, frames, key_padding_mask=None):
         """frames (n, N, d_slot) -> (n, N, d_slot); key_padding_mask (n, N) bool,
-        True = dead slot (ignored as a key)."""
+        True = dead slot (ignored as a key).  Replays a CUDA graph of the stack
+        (captured on first use of a frame-count bucket)."""
+        n = frames.shape[0]
+        if n == 0:
+            return frames.clone()
+        if not frames.is_cuda or torch.cuda.is_current_stream_capturing():
+            return self.forward(frames, key_padding_mask)
+        fin, kin, out, g = self.graph_slot(n, frames.shape[1], frames.shape[2], key_padding_mask is not None,
+                                           frames.dtype, frames.device)
+        fin[:n].copy_(frames)
+        if kin is not None:
+            kin[:n].copy_(key_padding_mask)
+        g.replay()
+        return out[:n].clone()
+
+    def graph_slot(self, n, N, Ds, has_kp, in_dtype, device):
+        """(static input, static key mask or None, static output, graph) for
+        n frames: the input and output hold a bucket of frames (n rounded up to
+        a multiple of 8); fill input[:n], replay, read output[:n] before the
+        next replay."""
+        nb = (n + 7) // 8 * 8
+        key = (nb, N, Ds, has_kp, in_dtype, str(device))
+        ent = self._graphs.get(key)
+        if ent is not None:
+            self._graphs.move_to_end(key)
+            return ent
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        fin = torch.zeros(nb, N, Ds, dtype=in_dtype, device=device)
+        kin = torch.zeros(nb, N, dtype=torch.bool, device=device) if has_kp else None
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            self.forward(fin, kin)  # first run outside the capture (library handles, workspaces)
+        torch.cuda.current_stream(device).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._pool):
+            out = self.forward(fin, kin)
+        ent = (fin, kin, out, g)
+        self._graphs[key] = ent
+        while len(self._graphs) > self.max_graphs:
+            self._graphs.popitem(last=False)
+        return ent
+
+    def forward(self, frames, key_padding_mask=None):
+        """The stack launched op by op (no graph)."""
         n, N, Ds = frames.shape
         if n == 0:
             return frames.clone()
@@ -182,13 +236,24 @@ def sparse_event_attention_fused(states, event_mask, transformer: EventTransform
     B, T, N, D = states.shape
     idx, pos, counts, meta = event_compact(event_mask)
     n = int(meta[0].item())  # one host read (the reference syncs for K_max too)
-    frames = event_gather(states, idx, counts, meta, n)
+    if n == 0:
+        return event_scatter(states, states[:0].reshape(0, N, D), pos, counts)
     kp = None
     if obj_mask is not None:
         dead = ~(obj_mask > 0.5)
         kp = dead[(idx[:n].long() // T)]
-    upd = transformer(frames, kp)
-    return event_scatter(states, upd.to(states.dtype), pos, counts)
+    if torch.cuda.is_current_stream_capturing():
+        frames = event_gather(states, idx, counts, meta, n)
+        upd = transformer.forward(frames, kp)
+        return event_scatter(states, upd.to(states.dtype), pos, counts)
+    # the frames are gathered straight into the graph's input, the graph runs
+    # the stack, and the scatter reads its output
+    fin, kin, out, g = transformer.graph_slot(n, N, D, kp is not None, states.dtype, states.device)
+    event_gather(states, idx, counts, meta, n, out=fin)
+    if kin is not None:
+        kin[:n].copy_(kp)
+    g.replay()
+    return event_scatter(states, out[:n], pos, counts)
 
 
 def sparse_event_attn_fn(states, event_mask, attn_fn, max_events=None, backend: str = "auto"):
