@@ -26,49 +26,60 @@ namespace hclsm {
 namespace event {
 
 // ---- compaction --------------------------------------------------------------------
-// One block walks the (B, T) mask in order.  Outputs: idx[k] = b*T + t of the
-// k-th fired frame (video-major, time ascending), pos[b*T + t] = k or -1,
-// counts[b] = fired frames of video b, meta[0] = total, meta[1] = max over videos.
+// One block scans the (B, T) mask as one flattened array: video-major, time
+// ascending, which is the order events are numbered in.  Outputs: idx[k] =
+// b*T + t of the k-th fired frame, pos[b*T + t] = k or -1, counts[b] = fired
+// frames of video b, meta[0] = total, meta[1] = max over videos.
 template <typename TM>
 __global__ void __launch_bounds__(1024) compact_kernel(const TM* __restrict__ mask, int B, int T,
                                                        int32_t* __restrict__ idx, int32_t* __restrict__ pos,
                                                        int32_t* __restrict__ counts, int32_t* __restrict__ meta) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_tot[32];
-  __shared__ int s_base, s_kmax;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) { s_base = 0; s_kmax = 0; }
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int64_t BT = (int64_t)B * T;
+  for (int b = tid; b < B; b += nthr) counts[b] = 0;
+  if (tid == 0) s_base = 0;
   __syncthreads();
-  for (int b = 0; b < B; ++b) {
-    int vid_count = 0;
-    for (int t0 = 0; t0 < T; t0 += 1024) {
-      const int t = t0 + tid;
-      const bool fired = t < T && static_cast<float>(mask[(int64_t)b * T + t]) > 0.5f;
-      const unsigned bal = __ballot_sync(0xffffffffu, fired);
-      if (lane == 0) warp_tot[warp] = __popc(bal);
-      __syncthreads();
-      int before = 0, tot = 0;
-      for (int w = 0; w < 32; ++w) {
-        const int c = warp_tot[w];
-        before += w < warp ? c : 0;
-        tot += c;
-      }
-      const int rank = s_base + before + __popc(bal & ((1u << lane) - 1u));
-      if (t < T) {
-        pos[(int64_t)b * T + t] = fired ? rank : -1;
-        if (fired) idx[rank] = b * T + t;
-      }
-      __syncthreads();
-      if (tid == 0) s_base += tot;
-      vid_count += tot;
-      __syncthreads();
+  for (int64_t i0 = 0; i0 < BT; i0 += nthr) {
+    const int64_t i = i0 + tid;
+    const bool fired = i < BT && static_cast<float>(mask[i]) > 0.5f;
+    const unsigned bal = __ballot_sync(0xffffffffu, fired);
+    if (lane == 0) warp_tot[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, tot = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) {
+      const int c = warp_tot[w];
+      before += w < warp ? c : 0;
+      tot += c;
     }
-    if (tid == 0) {
-      counts[b] = vid_count;
-      s_kmax = max(s_kmax, vid_count);
+    const int rank = s_base + before + __popc(bal & ((1u << lane) - 1u));
+    if (i < BT) {
+      pos[i] = fired ? rank : -1;
+      if (fired) {
+        idx[rank] = (int32_t)i;
+        atomicAdd(&counts[i / T], 1);
+      }
     }
+    __syncthreads();
+    if (tid == 0) s_base += tot;
+    __syncthreads();
   }
+  // largest per-video count
+  int m = 0;
+  for (int b = tid; b < B; b += nthr) m = max(m, counts[b]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) warp_tot[warp] = m;
   __syncthreads();
-  if (tid == 0) { meta[0] = s_base; meta[1] = s_kmax; }
+  if (tid == 0) {
+    int k = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) k = max(k, warp_tot[w]);
+    meta[0] = s_base;
+    meta[1] = k;
+  }
 }
 
 // out[k] = states[idx[k]] (frames of F elements, k < meta[0]); pad_k > 0 gives
@@ -339,14 +350,15 @@ extern "C" int hclsm_event_compact(const void* mask, int32_t mask_dtype, int32_t
     if (B > 0) cudaMemsetAsync(counts, 0, B * sizeof(int32_t), st);
     return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
   }
+  const int64_t BT = (int64_t)B * T;
+  const unsigned thr = (unsigned)std::min<int64_t>(1024, std::max<int64_t>(32, (BT + 31) / 32 * 32));
   if (mask_dtype == HCLSM_F32)
-    compact_kernel<float><<<1, 1024, 0, st>>>(static_cast<const float*>(mask), B, T, idx, pos, counts, meta);
-  else if (mask_dtype == HCLSM_BF16)
-    compact_kernel<__nv_bfloat16><<<1, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(mask), B, T, idx, pos,
-                                                      counts, meta);
-  else
-    return HCLSM_ERR_DTYPE;
-  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+    return launch_pdl(compact_kernel<float>, 1, thr, 0, st, static_cast<const float*>(mask), B, T, idx, pos, counts,
+                      meta);
+  if (mask_dtype == HCLSM_BF16)
+    return launch_pdl(compact_kernel<__nv_bfloat16>, 1, thr, 0, st, static_cast<const __nv_bfloat16*>(mask), B, T,
+                      idx, pos, counts, meta);
+  return HCLSM_ERR_DTYPE;
 }
 
 extern "C" int hclsm_event_gather(const void* states, const int32_t* idx, const int32_t* counts,

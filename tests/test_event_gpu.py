@@ -64,14 +64,18 @@ def test_known_answers(dtype):
     assert torch.equal(ident, st)
 
 
-def test_compaction_matches_nonzero_order():
+@pytest.mark.parametrize("B,T,p,mdtype", [(7, 300, 0.3, torch.float32), (8, 64, 0.1, torch.float32),
+                                          (3, 50, 0.0, torch.float32), (2, 40, 1.0, torch.float32),
+                                          (1, 1, 1.0, torch.float32), (3000, 5, 0.4, torch.float32),
+                                          (5, 700, 0.5, torch.bfloat16)])
+def test_compaction_matches_nonzero_order(B, T, p, mdtype):
     gen = torch.Generator().manual_seed(5)
-    m = (torch.rand(7, 300, generator=gen) < 0.3).float()
-    idx, pos, counts, meta = event_compact(m.cuda())
+    m = (torch.rand(B, T, generator=gen) < p).float()
+    idx, pos, counts, meta = event_compact(m.to(mdtype).cuda())
     nz = torch.nonzero(m.reshape(-1) > 0.5).flatten()
     n = int(meta[0])
     assert n == len(nz) and torch.equal(idx[:n].cpu().long(), nz)
-    assert torch.equal(counts[:7].cpu(), (m > 0.5).sum(1).int())
+    assert torch.equal(counts[:B].cpu(), (m > 0.5).sum(1).int())
     assert int(meta[1]) == int((m > 0.5).sum(1).max())
     p = pos.cpu()
     assert torch.equal(p[nz], torch.arange(n, dtype=torch.int32))
