@@ -153,6 +153,7 @@ class SlotIterationParams:
     ln_mlp_w: torch.Tensor
     ln_mlp_b: torch.Tensor
     scale: float
+    b1_bf16: torch.Tensor | None = None  # the MLP's first bias for the fused GEMM epilogue
 
     @classmethod
     def from_state(cls, sd: dict, device, d_slot: int | None = None):
@@ -163,10 +164,11 @@ class SlotIterationParams:
             return sd[name].detach().to(device=device, dtype=torch.float32).contiguous()
 
         D = d_slot or sd["project_q.weight"].shape[0]
+        b1 = f("mlp.0.bias")
         return cls(w("project_q.weight"), w("gru.weight_ih"), w("gru.weight_hh"), f("gru.bias_ih"),
-                   f("gru.bias_hh"), w("mlp.0.weight"), f("mlp.0.bias"), w("mlp.2.weight"), f("mlp.2.bias"),
+                   f("gru.bias_hh"), w("mlp.0.weight"), b1, w("mlp.2.weight"), f("mlp.2.bias"),
                    f("norm_pre_attn.weight"), f("norm_pre_attn.bias"), f("norm_slots.weight"),
-                   f("norm_slots.bias"), D ** -0.5)
+                   f("norm_slots.bias"), D ** -0.5, b1.to(torch.bfloat16))
 
     @classmethod
     def from_module(cls, mod):
@@ -192,7 +194,12 @@ def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_bf16=Non
     gh = _mm(slots_bf16.reshape(R, D), p.w_hh_t)
     h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
     m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=torch.bfloat16)
-    m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
+    if p.b1_bf16 is not None:
+        # bias + ReLU in the library GEMM's epilogue, bf16 out (the MLP runs in
+        # the autocast dtype in the reference)
+        m = torch._addmm_activation(p.b1_bf16, m, p.w1_t)
+    else:
+        m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
     m = _mm(m, p.w2_t)
     out_bf = torch.empty(R, D, dtype=torch.bfloat16, device=slots.device)
     out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_bf)
