@@ -42,6 +42,9 @@ SIGNATURES = {
     "hclsm_ssm_scan_fwd_states": (ctypes.c_int, [_vp] * 8 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp]),
     "hclsm_ssm_scan_bwd_states": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp,
                                                               _sz, _vp]),
+    "hclsm_l0_pool": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _i64, _vp]),
+    "hclsm_l0_epilogue": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _i64, _vp]),
+    "hclsm_l0_epilogue_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _vp, _i32, _i32, _i64, _vp]),
     "hclsm_slot_attn_core": (ctypes.c_int, [_vp] * 5 + [_i32] * 4 + [ctypes.c_float] * 3 + [_i32, _i32, _vp]),
     "hclsm_layernorm": (ctypes.c_int, [_vp] * 4 + [_i64, _i32, ctypes.c_float, _i32, _vp]),
     "hclsm_gru_cell": (ctypes.c_int, [_vp] * 6 + [_i64, _i32, _vp]),

@@ -12,6 +12,8 @@ What is replaced (paths inside RightNow-AI/hclsm):
   softplus(dt_proj(z)) with its clamp, the inline clamped scan and the SiLU
   gate run as one differentiable kernel call (clamp=True, dt_softplus=True,
   z = gate_proj(x));
+* ``Level0SSM.forward`` (hclsm/dynamics/level0_ssm.py:159-220): the masked
+  mean over objects and the nan_to_num / clamp / mask epilogue as kernels;
 * ``DynamicSlotAttention._iteration_step`` (hclsm/objects/dynamic_slots.py:98-131);
 * ``HierarchyManager.gather_events`` / ``scatter_events``
   (hclsm/dynamics/hierarchy_manager.py:42-118);
@@ -175,6 +177,14 @@ def install(hclsm_module=None):
     if l0 is not None and hasattr(l0, "SimplifiedSSMBlock"):
         _patch(l0.SimplifiedSSMBlock, "forward", _ssm_block_forward)
         done.append("SimplifiedSSMBlock.forward")
+    if l0 is not None and hasattr(l0, "Level0SSM"):
+        from .kernels.level0 import level0_forward
+
+        def _level0(self, obj_states, obj_mask=None):
+            return level0_forward(self, obj_states, obj_mask)
+
+        _patch(l0.Level0SSM, "forward", _level0)
+        done.append("Level0SSM.forward")
     ds = getattr(obj, "dynamic_slots", None) if obj is not None else None
     if ds is not None and hasattr(ds, "DynamicSlotAttention"):
         cls = ds.DynamicSlotAttention

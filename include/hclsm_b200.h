@@ -123,6 +123,23 @@ int hclsm_ssm_scan_bwd_states(const void* x, const void* dt, const float* A_log,
                               size_t states_bytes, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Level0SSM around its blocks (hclsm/dynamics/level0_ssm.py:159-220).
+ *   obj / x : (B, N, T*D) contiguous, obj_dtype / x_dtype f32 or bf16
+ *   mask    : (B, N) f32, optional (NULL)
+ * hclsm_l0_pool: out (B, T*D) = sum_n mask obj / max(sum_n mask, 1), or the
+ *   mean over n without a mask (the global track's input, :175-180).
+ * hclsm_l0_epilogue: out = clamp(nan_to_num(x, 0, 100, -100), -100, 100) * mask
+ *   in one pass (:210-218).
+ * hclsm_l0_epilogue_bwd: gx (x's dtype) = g * mask * [x finite, |x| <= 100].
+ * ------------------------------------------------------------------------- */
+int hclsm_l0_pool(const void* obj, int32_t obj_dtype, const float* mask, void* out, int32_t out_dtype, int32_t B,
+                  int32_t N, int64_t TD, void* stream);
+int hclsm_l0_epilogue(const void* x, int32_t x_dtype, const float* mask, void* out, int32_t out_dtype, int32_t B,
+                      int32_t N, int64_t TD, void* stream);
+int hclsm_l0_epilogue_bwd(const void* x, int32_t x_dtype, const float* mask, const void* g, int32_t g_dtype,
+                          void* gx, int32_t B, int32_t N, int64_t TD, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Slot attention core: out = softmax_over_slots(clamp(Q K^T * scale)) V.
  * Replaces hclsm/kernels/slot_attention_kernel.py:324 slot_attention_fn (the
  * arithmetic of naive_slot_attention :265-291 with eps=0, of the Triton path

@@ -120,6 +120,43 @@ def block_cases():
     return out
 
 
+def level0_cases():
+    """Level0SSM forward and gradients (hclsm/dynamics/level0_ssm.py:126-220)
+    with SimplifiedSSMBlocks, a mask with dead objects and inputs large enough
+    that the epilogue's +-100 clamp binds; and the same module without a mask."""
+    from hclsm.config import Level0Config
+    from hclsm.dynamics.level0_ssm import Level0SSM
+
+    g = torch.Generator().manual_seed(600)
+    mod = Level0SSM(Level0Config(d_state=16, n_blocks=2, expand_ratio=2), d_slot=32)
+    with torch.no_grad():
+        for name, p in mod.named_parameters():
+            if "norm" in name:
+                continue
+            if name.endswith("A_log"):
+                p.copy_(torch.empty(p.shape).uniform_(-1.0, 0.5, generator=g))
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.2)
+    out = {}
+    for case, use_mask in (("l0m", True), ("l0", False)):
+        x = torch.randn(2, 3, 10, 32, generator=g)
+        x[0, 0, 4, :6] = 400.0  # carried by the residuals past the clamp
+        x.requires_grad_(True)
+        mask = torch.tensor([[1.0, 1.0, 0.0], [1.0, 0.0, 1.0]]) if use_mask else None
+        dy = torch.randn(2, 3, 10, 32, generator=g)
+        mod.zero_grad()
+        y = mod(x, mask)
+        y.backward(dy)
+        out.update({f"{case}/x": _np(x), f"{case}/dy": _np(dy), f"{case}/y": _np(y), f"{case}/dx": _np(x.grad)})
+        if mask is not None:
+            out[f"{case}/mask"] = _np(mask)
+        for name, p in mod.named_parameters():
+            out[f"{case}/g/{name}"] = _np(p.grad)
+    for name, p in mod.named_parameters():
+        out[f"l0w/{name}"] = _np(p)
+    return out
+
+
 def slot_cases():
     from hclsm.kernels.slot_attention_kernel import naive_slot_attention
     from hclsm.config import ObjectConfig
@@ -208,12 +245,18 @@ def event_cases():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default=None, help="write only this fixture (scan, slot, event, level0)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(1)
+    if args.only == "level0":
+        np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
+        print("wrote level0_golden.npz")
+        return
     np.savez_compressed(os.path.join(HERE, "scan_golden.npz"), **scan_cases(), **block_cases())
     np.savez_compressed(os.path.join(HERE, "slot_golden.npz"), **slot_cases())
     np.savez_compressed(os.path.join(HERE, "event_golden.npz"), **event_cases())
+    np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

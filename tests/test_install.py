@@ -42,10 +42,14 @@ def _fake_hclsm():
         def forward(self, e, p=None, o=None):
             return "reference"
 
+    class L0:
+        def forward(self, s, m=None):
+            return "reference"
+
     kernels = mod(ssm_scan_fn=f, slot_attention_fn=f, sparse_event_attn_fn=f,
                   ssm_scan_kernel=mod(ssm_scan_fn=f), slot_attention_kernel=mod(slot_attention_fn=f),
                   sparse_event_attn=mod(sparse_event_attn_fn=f))
-    dyn = mod(level0_ssm=mod(SimplifiedSSMBlock=Block), hierarchy_manager=mod(HierarchyManager=HM),
+    dyn = mod(level0_ssm=mod(SimplifiedSSMBlock=Block, Level0SSM=L0), hierarchy_manager=mod(HierarchyManager=HM),
               level1_event=mod(Level1EventDynamics=L1))
     objs = mod(dynamic_slots=mod(DynamicSlotAttention=DSA))
     return mod(kernels=kernels, dynamics=dyn, objects=objs), (Block, DSA, HM, L1)
@@ -56,7 +60,7 @@ def test_install_patches_and_uninstall_restores():
     orig = Block.forward
     done = inst.install(pkg)
     done2 = inst.install(pkg)  # idempotent
-    assert done == done2 and len(done) == 11
+    assert done == done2 and len(done) == 12
     assert pkg.kernels.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert pkg.kernels.ssm_scan_kernel.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert Block.forward is not orig
