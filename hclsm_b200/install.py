@@ -15,6 +15,9 @@ What is replaced (paths inside RightNow-AI/hclsm):
 * ``Level0SSM.forward`` (hclsm/dynamics/level0_ssm.py:159-220): the masked
   mean over objects and the nan_to_num / clamp / mask epilogue as kernels;
 * ``DynamicSlotAttention._iteration_step`` (hclsm/objects/dynamic_slots.py:98-131);
+* ``DynamicSlotAttention.forward`` (hclsm/objects/dynamic_slots.py:133-203):
+  slot birth decided and written on the device (no host read of
+  ``needs_birth``, no per-video Python loop);
 * ``HierarchyManager.gather_events`` / ``scatter_events``
   (hclsm/dynamics/hierarchy_manager.py:42-118);
 * ``Level1EventDynamics.forward`` (hclsm/dynamics/level1_event.py:85-133).
@@ -89,6 +92,49 @@ def _make_iteration_step(orig):
         return out.to(slots.dtype)
 
     return _iteration_step
+
+
+def _make_dsa_forward(orig):
+    def forward(self, inputs, return_attention=False):
+        """DynamicSlotAttention.forward (dynamic_slots.py:133-203) with the
+        birth step on the device: per video, the token of largest residual
+        attention energy and the first dormant slot are found by argmax, the
+        birth projection runs for every video, and torch.where keeps it only
+        where the reference would write it (energy above the threshold and a
+        dormant slot present).  No host synchronisation."""
+        import torch.nn.functional as F
+        import torch.utils.checkpoint
+
+        B, M, _ = inputs.shape
+        inputs_norm = self.norm_input(inputs)
+        k = self.project_k(inputs_norm)
+        v = self.project_v(inputs_norm)
+        slots = self._init_slots(B, inputs.device)
+        for _ in range(self.n_iterations):
+            if self.use_gradient_checkpointing and self.training:
+                slots = torch.utils.checkpoint.checkpoint(self._iteration_step, slots, k, v, use_reentrant=False)
+            else:
+                slots = self._iteration_step(slots, k, v)
+        alive = torch.sigmoid(self.existence_head(slots).squeeze(-1))
+        with torch.no_grad():
+            q = self.project_q(self.norm_pre_attn(slots))
+            attn = F.softmax(torch.bmm(q, k.transpose(1, 2)) * self.scale, dim=1)
+            final_attn = attn if return_attention else None
+            residual = (1.0 - attn.sum(dim=1)).abs()
+            max_residual = residual.max(dim=-1).values
+            token = residual.argmax(dim=-1)
+            dormant = alive < self.existence_threshold
+            birth = (max_residual > self.birth_threshold) & dormant.any(dim=1)
+            first = dormant.to(torch.int8).argmax(dim=1)  # first dormant slot (argmax returns the first maximum)
+            ar = torch.arange(B, device=inputs.device)
+            born = self.birth_proj(inputs[ar, token]).to(slots.dtype)
+            sel = birth[:, None] & (torch.arange(slots.shape[1], device=inputs.device)[None, :] == first[:, None])
+        slots = torch.where(sel[:, :, None], born[:, None, :], slots)
+        if return_attention:
+            return slots, alive, final_attn
+        return slots, alive
+
+    return forward
 
 
 def _make_gather(orig):
@@ -189,7 +235,8 @@ def install(hclsm_module=None):
     if ds is not None and hasattr(ds, "DynamicSlotAttention"):
         cls = ds.DynamicSlotAttention
         _patch(cls, "_iteration_step", _make_iteration_step(_orig(cls, "_iteration_step")))
-        done.append("DynamicSlotAttention._iteration_step")
+        _patch(cls, "forward", _make_dsa_forward(_orig(cls, "forward")))
+        done += ["DynamicSlotAttention._iteration_step", "DynamicSlotAttention.forward"]
     hm = getattr(dyn, "hierarchy_manager", None) if dyn is not None else None
     if hm is not None and hasattr(hm, "HierarchyManager"):
         cls = hm.HierarchyManager

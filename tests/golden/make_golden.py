@@ -157,6 +157,44 @@ def level0_cases():
     return out
 
 
+def dsa_cases():
+    """DynamicSlotAttention.forward (hclsm/objects/dynamic_slots.py:133-203)
+    under no_grad with fixed initial slots (the module's _init_slots replaced,
+    its draw is random), 3 iterations, the existence head, and slot birth.  With
+    the softmax over slots every token receives attention 1 up to rounding, so
+    the birth energy is rounding noise: birth_threshold -1 forces births (the
+    token chosen is arbitrary), 0.7 (the default) never births."""
+    from hclsm.config import ObjectConfig
+    from hclsm.objects.dynamic_slots import DynamicSlotAttention
+
+    out = {}
+    for case, thr, seed0 in (("dsa_birth", -1.0, 700), ("dsa", 0.7, 800)):
+        # the first seed whose existence probabilities all sit at least 0.1
+        # from the threshold, so bf16 rounding cannot flip a dormant decision
+        for seed in range(seed0, seed0 + 100):
+            g = torch.Generator().manual_seed(seed)
+            cfg = ObjectConfig(d_slot=32, n_max_slots=6, n_iterations=3, existence_threshold=0.5,
+                               birth_threshold=thr)
+            mod = DynamicSlotAttention(cfg, d_input=24)
+            with torch.no_grad():
+                for name, p in mod.named_parameters():
+                    if "norm" in name:
+                        continue
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.2)
+            slots0 = torch.randn(3, 6, 32, generator=g) * 0.5
+            mod._init_slots = lambda B, device, s0=slots0: s0.clone()
+            inputs = torch.randn(3, 10, 24, generator=g)
+            with torch.no_grad():
+                slots, alive, attn = mod(inputs, return_attention=True)
+            if float((alive - 0.5).abs().min()) > 0.1 and bool((alive < 0.5).any()):
+                break
+        out.update({f"{case}/inputs": _np(inputs), f"{case}/slots0": _np(slots0), f"{case}/slots": _np(slots),
+                    f"{case}/alive": _np(alive), f"{case}/attn": _np(attn), f"{case}/thr": np.array(thr)})
+        for name, p in mod.named_parameters():
+            out[f"{case}/w/{name}"] = _np(p)
+    return out
+
+
 def slot_cases():
     from hclsm.kernels.slot_attention_kernel import naive_slot_attention
     from hclsm.config import ObjectConfig
@@ -245,7 +283,7 @@ def event_cases():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", default=None, help="write only this fixture (scan, slot, event, level0)")
+    ap.add_argument("--only", default=None, help="write only this fixture (level0, dsa)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(1)
@@ -253,10 +291,15 @@ def main():
         np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
         print("wrote level0_golden.npz")
         return
+    if args.only == "dsa":
+        np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
+        print("wrote dsa_golden.npz")
+        return
     np.savez_compressed(os.path.join(HERE, "scan_golden.npz"), **scan_cases(), **block_cases())
     np.savez_compressed(os.path.join(HERE, "slot_golden.npz"), **slot_cases())
     np.savez_compressed(os.path.join(HERE, "event_golden.npz"), **event_cases())
     np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
+    np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

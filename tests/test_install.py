@@ -31,6 +31,9 @@ def _fake_hclsm():
         def _iteration_step(self, s, k, v):
             return "reference"
 
+        def forward(self, inputs, return_attention=False):
+            return "reference"
+
     class HM:
         def gather_events(self, s, m):
             return "reference"
@@ -60,7 +63,7 @@ def test_install_patches_and_uninstall_restores():
     orig = Block.forward
     done = inst.install(pkg)
     done2 = inst.install(pkg)  # idempotent
-    assert done == done2 and len(done) == 12
+    assert done == done2 and len(done) == 13
     assert pkg.kernels.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert pkg.kernels.ssm_scan_kernel.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert Block.forward is not orig
