@@ -50,6 +50,7 @@ SIGNATURES = {
     "hclsm_gru_cell": (ctypes.c_int, [_vp] * 6 + [_i64, _i32, _vp]),
     "hclsm_bias_act": (ctypes.c_int, [_vp] * 3 + [_i64, _i32, _i32, _i32, _vp]),
     "hclsm_residual_clamp": (ctypes.c_int, [_vp] * 5 + [_i64, _i32, ctypes.c_float, _vp]),
+    "hclsm_event_detect": (ctypes.c_int, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "hclsm_event_compact": (ctypes.c_int, [_vp, _i32, _i32, _i32] + [_vp] * 5),
     "hclsm_event_gather": (ctypes.c_int, [_vp] * 5 + [_i64, _i32, _i32, _i64, _i32, _vp]),
     "hclsm_event_scatter": (ctypes.c_int, [_vp] * 5 + [_i64, _i64, _i32, _i32, _i32, _vp]),

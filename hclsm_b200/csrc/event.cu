@@ -82,6 +82,78 @@ __global__ void __launch_bounds__(1024) compact_kernel(const TM* __restrict__ ma
   }
 }
 
+// EventDetector's decision (hclsm/dynamics/event_detector.py:162-170) and the
+// compaction in one block: hard[b, t] = probs[b, t] > *threshold; if any video
+// has no event, t = 0 is made an event in every video (the reference's
+// "always keep at least one event", decided there by a host read); then the
+// same flattened scan as compact_kernel.  meta[2] = 1 when that rule fired.
+__global__ void __launch_bounds__(1024) detect_kernel(const float* __restrict__ probs,
+                                                      const float* __restrict__ threshold, int B, int T,
+                                                      float* __restrict__ hard, int32_t* __restrict__ idx,
+                                                      int32_t* __restrict__ pos, int32_t* __restrict__ counts,
+                                                      int32_t* __restrict__ meta) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int warp_tot[32];
+  __shared__ int s_base, s_empty;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int64_t BT = (int64_t)B * T;
+  const float thr = *threshold;
+  for (int b = tid; b < B; b += nthr) counts[b] = 0;
+  if (tid == 0) { s_base = 0; s_empty = 0; }
+  __syncthreads();
+  for (int64_t i = tid; i < BT; i += nthr)
+    if (probs[i] > thr) atomicAdd(&counts[i / T], 1);
+  __syncthreads();
+  for (int b = tid; b < B; b += nthr)
+    if (counts[b] == 0) s_empty = 1;
+  __syncthreads();
+  const bool force0 = s_empty != 0;
+  for (int b = tid; b < B; b += nthr) counts[b] = 0;
+  __syncthreads();
+  for (int64_t i0 = 0; i0 < BT; i0 += nthr) {
+    const int64_t i = i0 + tid;
+    bool fired = false;
+    if (i < BT) {
+      fired = probs[i] > thr || (force0 && i % T == 0);
+      hard[i] = fired ? 1.0f : 0.0f;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, fired);
+    if (lane == 0) warp_tot[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, tot = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) {
+      const int c = warp_tot[w];
+      before += w < warp ? c : 0;
+      tot += c;
+    }
+    const int rank = s_base + before + __popc(bal & ((1u << lane) - 1u));
+    if (i < BT) {
+      pos[i] = fired ? rank : -1;
+      if (fired) {
+        idx[rank] = (int32_t)i;
+        atomicAdd(&counts[i / T], 1);
+      }
+    }
+    __syncthreads();
+    if (tid == 0) s_base += tot;
+    __syncthreads();
+  }
+  int m = 0;
+  for (int b = tid; b < B; b += nthr) m = max(m, counts[b]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) warp_tot[warp] = m;
+  __syncthreads();
+  if (tid == 0) {
+    int k = 0;
+    for (int w = 0; w < (nthr >> 5); ++w) k = max(k, warp_tot[w]);
+    meta[0] = s_base;
+    meta[1] = k;
+    meta[2] = force0 ? 1 : 0;
+  }
+}
+
 // out[k] = states[idx[k]] (frames of F elements, k < meta[0]); pad_k > 0 gives
 // the padded (B, pad_k) layout instead: out[b, j] = j-th event of video b or 0.
 template <typename T>
@@ -359,6 +431,16 @@ extern "C" int hclsm_event_compact(const void* mask, int32_t mask_dtype, int32_t
     return launch_pdl(compact_kernel<__nv_bfloat16>, 1, thr, 0, st, static_cast<const __nv_bfloat16*>(mask), B, T,
                       idx, pos, counts, meta);
   return HCLSM_ERR_DTYPE;
+}
+
+extern "C" int hclsm_event_detect(const float* probs, const float* threshold, int32_t B, int32_t T, float* hard,
+                                  int32_t* idx, int32_t* pos, int32_t* counts, int32_t* meta, void* stream) {
+  if (!probs || !threshold || !hard || !idx || !pos || !counts || !meta) return HCLSM_ERR_NULL;
+  if (B <= 0 || T <= 0) return HCLSM_ERR_SHAPE;
+  const int64_t BT = (int64_t)B * T;
+  const unsigned thr = (unsigned)std::min<int64_t>(1024, std::max<int64_t>(32, (BT + 31) / 32 * 32));
+  return launch_pdl(detect_kernel, 1, thr, 0, static_cast<cudaStream_t>(stream), probs, threshold, B, T, hard, idx,
+                    pos, counts, meta);
 }
 
 extern "C" int hclsm_event_gather(const void* states, const int32_t* idx, const int32_t* counts,

@@ -18,6 +18,9 @@ What is replaced (paths inside RightNow-AI/hclsm):
 * ``DynamicSlotAttention.forward`` (hclsm/objects/dynamic_slots.py:133-203):
   slot birth decided and written on the device (no host read of
   ``needs_birth``, no per-video Python loop);
+* ``EventDetector.forward`` (hclsm/dynamics/event_detector.py:133-172): the
+  hard decision, the "at least one event" rule and the compaction in one
+  kernel (no host read), handed to the gather / scatter through the mask;
 * ``HierarchyManager.gather_events`` / ``scatter_events``
   (hclsm/dynamics/hierarchy_manager.py:42-118);
 * ``Level1EventDynamics.forward`` (hclsm/dynamics/level1_event.py:85-133).
@@ -145,8 +148,11 @@ def _make_gather(orig):
 
         B, T, N, D = states.shape
         st = states.contiguous()
-        idx, pos, counts, meta = event_compact(event_mask)
+        cached = getattr(event_mask, "_hclsm_events", None)  # from the patched EventDetector
+        idx, pos, counts, meta = cached if cached is not None else event_compact(event_mask)
         kmax = max(int(meta[1].item()), 1)
+        if cached is not None:
+            event_mask._hclsm_kmax = kmax
         ev = event_gather(st, idx, counts, meta, B * kmax, pad_k=kmax).reshape(B, kmax, N, D)
         pad = (torch.arange(kmax, device=states.device)[None, :] < counts[:B, None]).float()
         return ev, pad, kmax
@@ -161,13 +167,41 @@ def _make_scatter(orig):
         from .kernels.sparse_event_attn import event_compact, event_scatter
 
         K = event_updates.shape[1]
-        m = (event_mask > 0.5)
-        rank = torch.cumsum(m.int(), dim=1) - 1
-        idx, pos, counts, meta = event_compact((m & (rank < K)).float())
+        cached = getattr(event_mask, "_hclsm_events", None)
+        if cached is not None and K >= getattr(event_mask, "_hclsm_kmax", K + 1):
+            idx, pos, counts, meta = cached  # every event fits: the detector's compaction as is
+        else:
+            m = (event_mask > 0.5)
+            rank = torch.cumsum(m.int(), dim=1) - 1
+            idx, pos, counts, meta = event_compact((m & (rank < K)).float())
         upd = event_updates.reshape(-1, *event_updates.shape[2:]).to(base_states.dtype).contiguous()
         return event_scatter(base_states.contiguous(), upd, pos, counts, pad_k=K)
 
     return scatter_events
+
+
+def _make_detector_forward(orig):
+    def forward(self, states):
+        """EventDetector.forward (event_detector.py:133-172): the module's own
+        temporal features, causal dilated convolutions and head, then the
+        decision and compaction on the device (no host read)."""
+        import torch.nn.functional as F
+        from .kernels.sparse_event_attn import event_detect
+
+        B, T, D = states.shape
+        temporal_feat = self.temporal_features(states)
+        x = temporal_feat.transpose(1, 2)
+        h = F.relu(self.conv1(x))[:, :, :T]
+        h = F.relu(self.conv2(h))[:, :, :T]
+        h = F.relu(self.conv3(h))[:, :, :T]
+        conv_out = self.norm(h.transpose(1, 2))
+        combined = torch.cat([conv_out, temporal_feat], dim=-1)
+        event_probs = torch.sigmoid(self.head(combined).squeeze(-1))
+        if not event_probs.is_cuda:
+            return orig(self, states)
+        return event_probs, event_detect(event_probs, self.learned_threshold)
+
+    return forward
 
 
 def _make_level1_forward(orig):
@@ -243,6 +277,11 @@ def install(hclsm_module=None):
         _patch(cls, "gather_events", _make_gather(_orig(cls, "gather_events")))
         _patch(cls, "scatter_events", _make_scatter(_orig(cls, "scatter_events")))
         done += ["HierarchyManager.gather_events", "HierarchyManager.scatter_events"]
+    ed = getattr(dyn, "event_detector", None) if dyn is not None else None
+    if ed is not None and hasattr(ed, "EventDetector"):
+        cls = ed.EventDetector
+        _patch(cls, "forward", _make_detector_forward(_orig(cls, "forward")))
+        done.append("EventDetector.forward")
     l1 = getattr(dyn, "level1_event", None) if dyn is not None else None
     if l1 is not None and hasattr(l1, "Level1EventDynamics"):
         cls = l1.Level1EventDynamics

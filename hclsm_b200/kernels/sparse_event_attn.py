@@ -25,7 +25,7 @@ import torch
 from .. import _lib
 from .slot_attention_kernel import layernorm, residual_clamp
 
-__all__ = ["sparse_event_attn_fn", "EventTransformer", "event_compact", "event_gather", "event_scatter",
+__all__ = ["sparse_event_attn_fn", "EventTransformer", "event_compact", "event_detect", "event_gather", "event_scatter",
            "sparse_event_attention_fused"]
 
 
@@ -55,6 +55,40 @@ def event_compact(event_mask):
                                          _lib.ptr(counts), _lib.ptr(meta), _lib.stream_ptr(dev))
     _lib.check(rc, "hclsm_event_compact")
     return idx, pos, counts, meta
+
+
+def event_detect(event_probs, threshold):
+    """EventDetector's mask from its probabilities (event_detector.py:162-170)
+    with the decision and the compaction on the device: hard = probs >
+    threshold (a tensor, read on the device), the straight-through mask
+    hard - probs.detach() + probs, and, when any video has no event, t = 0
+    set to 1 in every video (the reference decides that with a host read).
+    The compaction (idx, pos, counts, meta) of the final mask is attached to
+    the returned mask as ``_hclsm_events`` for the gather and the scatter."""
+    _lib.require_cuda(event_probs, threshold)
+    B, T = event_probs.shape
+    dev = event_probs.device
+    p = _c(event_probs.detach().to(torch.float32))
+    thr = _c(threshold.detach().to(torch.float32).reshape(-1)[:1])
+    hard = torch.empty(B, T, dtype=torch.float32, device=dev)
+    idx = torch.empty(B * T, dtype=torch.int32, device=dev)
+    pos = torch.empty(B * T, dtype=torch.int32, device=dev)
+    counts = torch.empty(B, dtype=torch.int32, device=dev)
+    meta = torch.empty(3, dtype=torch.int32, device=dev)
+    rc = _lib.load().hclsm_event_detect(_lib.ptr(p), _lib.ptr(thr), B, T, _lib.ptr(hard), _lib.ptr(idx),
+                                        _lib.ptr(pos), _lib.ptr(counts), _lib.ptr(meta), _lib.stream_ptr(dev))
+    _lib.check(rc, "hclsm_event_detect")
+    mask = hard.to(event_probs.dtype) - event_probs.detach() + event_probs
+    first = torch.zeros(B, T, dtype=torch.bool, device=dev)
+    first[:, 0] = True
+    mask = torch.where(first & (meta[2] > 0), torch.ones((), dtype=mask.dtype, device=dev), mask)
+    mask._hclsm_events = (idx, pos, counts, meta)
+    return mask
+
+
+def _cached_compaction(event_mask):
+    """The compaction event_detect attached to this mask, or None."""
+    return getattr(event_mask, "_hclsm_events", None)
 
 
 def event_gather(states, idx, counts, meta, n_frames, pad_k=0, out=None):

@@ -204,6 +204,16 @@ int hclsm_event_mha(const void* qkv, const uint8_t* key_pad, void* out, int32_t 
                     int32_t HD, float scale, int32_t dtype, void* stream);
 int hclsm_swiglu(const float* u, void* y, int64_t rows, int32_t C, int32_t out_dtype, void* stream);
 
+/* EventDetector's hard decision and the compaction in one launch
+ * (hclsm/dynamics/event_detector.py:162-170 feeding hierarchy_manager.py:42-77):
+ * hard[b, t] = probs[b, t] > *threshold (f32, the learned threshold read on the
+ * device); if any video has no event, t = 0 becomes an event in every video
+ * (the reference's rule, decided there by a host read); idx / pos / counts as
+ * hclsm_event_compact, meta[0] = events, meta[1] = max per video, meta[2] = 1
+ * when the t = 0 rule fired (meta holds 3 ints).  probs and hard (B, T) f32. */
+int hclsm_event_detect(const float* probs, const float* threshold, int32_t B, int32_t T, float* hard, int32_t* idx,
+                       int32_t* pos, int32_t* counts, int32_t* meta, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Selective SSM scan, backward, without a caller workspace.
  * No counterpart in the reference: an addition for callers that cannot

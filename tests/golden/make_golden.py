@@ -195,6 +195,43 @@ def dsa_cases():
     return out
 
 
+def detector_cases():
+    """EventDetector.forward (hclsm/dynamics/event_detector.py:133-172): its
+    probabilities, the straight-through mask and the gradient of sum(mask * w)
+    with respect to the probabilities; "ed0" has a video without an event (the
+    t = 0 rule fires), "ed1" does not."""
+    from hclsm.dynamics.event_detector import EventDetector
+
+    out = {}
+    for case, want_empty, seed0 in (("ed0", True, 900), ("ed1", False, 950)):
+        for seed in range(seed0, seed0 + 200):
+            g = torch.Generator().manual_seed(seed)
+            det = EventDetector(d_input=16, threshold=0.5)
+            with torch.no_grad():
+                for name, p in det.named_parameters():
+                    if name == "threshold_logit" or "norm" in name:
+                        continue
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.4)
+            states = torch.randn(4, 12, 16, generator=g)
+            probs, mask = det(states)
+            thr = float(det.learned_threshold.detach())
+            empty = bool(((probs > thr).sum(dim=1) == 0).any())
+            margin = float((probs - thr).abs().min())
+            if empty == want_empty and margin > 1e-3:
+                break
+        probs_leaf = probs.detach().clone().requires_grad_(True)
+        hard = (probs_leaf > thr).float()
+        m2 = hard - probs_leaf.detach() + probs_leaf
+        if hard.sum(dim=1).min() == 0:
+            m2 = m2.clone()
+            m2[:, 0] = 1.0
+        w = torch.randn(4, 12, generator=g)
+        (m2 * w).sum().backward()
+        out.update({f"{case}/probs": _np(probs), f"{case}/mask": _np(mask), f"{case}/thr": np.array(thr, np.float32),
+                    f"{case}/w": _np(w), f"{case}/dprobs": _np(probs_leaf.grad)})
+    return out
+
+
 def slot_cases():
     from hclsm.kernels.slot_attention_kernel import naive_slot_attention
     from hclsm.config import ObjectConfig
@@ -283,13 +320,17 @@ def event_cases():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", default=None, help="write only this fixture (level0, dsa)")
+    ap.add_argument("--only", default=None, help="write only this fixture (level0, dsa, detector)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(1)
     if args.only == "level0":
         np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
         print("wrote level0_golden.npz")
+        return
+    if args.only == "detector":
+        np.savez_compressed(os.path.join(HERE, "detector_golden.npz"), **detector_cases())
+        print("wrote detector_golden.npz")
         return
     if args.only == "dsa":
         np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
@@ -300,6 +341,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "event_golden.npz"), **event_cases())
     np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
     np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
+    np.savez_compressed(os.path.join(HERE, "detector_golden.npz"), **detector_cases())
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -105,3 +105,83 @@ def test_config3_bf16_vs_oracle():
     # non-event frames are bit-identical copies
     nz = d["mask"] < 0.5
     assert torch.equal(y.cpu()[nz], st[nz])
+
+
+DET_GOLD = os.path.join(os.path.dirname(__file__), "golden", "detector_golden.npz")
+
+
+def _ref_detector_tail(probs, thr):
+    hard = (probs > thr).float()
+    mask = hard - probs.detach() + probs
+    if hard.sum(dim=1).min() == 0:
+        mask = mask.clone()
+        mask[:, 0] = 1.0
+    return mask
+
+
+@pytest.mark.parametrize("case", ["ed0", "ed1"])
+def test_detector_tail_matches_reference_golden(case):
+    """EventDetector's mask (event_detector.py:162-170) from the reference's
+    own probabilities: bit-identical mask, gradient to the probabilities, and
+    the attached compaction equals that of the mask."""
+    from hclsm_b200.kernels.sparse_event_attn import event_detect
+    g = np.load(DET_GOLD)
+    probs = torch.from_numpy(g[f"{case}/probs"]).cuda().requires_grad_(True)
+    thr = torch.tensor([float(g[f"{case}/thr"])], device="cuda")
+    mask = event_detect(probs, thr)
+    assert torch.equal(mask.detach().cpu(), torch.from_numpy(g[f"{case}/mask"]))
+    (mask * torch.from_numpy(g[f"{case}/w"]).cuda()).sum().backward()
+    assert torch.equal(probs.grad.cpu(), torch.from_numpy(g[f"{case}/dprobs"]))
+    idx, pos, counts, meta = mask._hclsm_events
+    ref = event_compact(mask.detach())
+    n = int(ref[3][0])
+    assert int(meta[0]) == n and int(meta[1]) == int(ref[3][1])
+    assert torch.equal(idx[:n], ref[0][:n]) and torch.equal(pos, ref[1]) and torch.equal(counts, ref[2])
+
+
+@pytest.mark.parametrize("B,T,empty_rows", [(8, 64, []), (8, 64, [3]), (5, 300, [0, 4]), (3, 7, [0, 1, 2]),
+                                            (1200, 3, [7])])
+def test_detector_tail_vs_torch(B, T, empty_rows):
+    from hclsm_b200.kernels.sparse_event_attn import event_detect
+    gen = torch.Generator().manual_seed(B * T)
+    probs = torch.rand(B, T, generator=gen)
+    for r in empty_rows:
+        probs[r] = probs[r] * 0.4  # below the threshold everywhere
+    probs = probs.cuda().requires_grad_(True)
+    p2 = probs.detach().clone().requires_grad_(True)
+    thr = torch.tensor([0.6], device="cuda")
+    mask = event_detect(probs, thr)
+    ref = _ref_detector_tail(p2, 0.6)
+    assert torch.equal(mask, ref)
+    w = torch.randn(B, T, generator=gen).cuda()
+    (mask * w).sum().backward()
+    (ref * w).sum().backward()
+    assert torch.equal(probs.grad, p2.grad)
+    idx, pos, counts, meta = mask._hclsm_events
+    assert int(meta[2]) == (1 if empty_rows else 0)
+    nz = torch.nonzero(ref.detach().reshape(-1) > 0.5).flatten()
+    assert int(meta[0]) == len(nz) and torch.equal(idx[: len(nz)].long(), nz)
+
+
+def test_gather_scatter_use_the_detector_compaction():
+    """The patched HierarchyManager.gather_events / scatter_events give the
+    same results from the compaction the detector attached as from their own."""
+    from hclsm_b200 import install as inst
+    from hclsm_b200.kernels.sparse_event_attn import event_detect
+    gen = torch.Generator().manual_seed(9)
+    probs = torch.rand(6, 20, generator=gen).cuda()
+    probs[2] *= 0.3
+    mask = event_detect(probs, torch.tensor([0.7], device="cuda"))
+    plain = mask.detach().clone()
+    assert getattr(plain, "_hclsm_events", None) is None
+    states = torch.randn(6, 20, 4, 16, generator=gen).cuda()
+    gather = inst._make_gather(None)
+    scatter = inst._make_scatter(None)
+    with torch.no_grad():
+        e1, p1, k1 = gather(None, states, mask)
+        e2, p2, k2 = gather(None, states, plain)
+        assert k1 == k2 and torch.equal(e1, e2) and torch.equal(p1, p2)
+        upd = torch.randn(e1.shape, generator=gen).cuda()
+        s1 = scatter(None, states, upd, mask)
+        s2 = scatter(None, states, upd, plain)
+        assert torch.equal(s1, s2)

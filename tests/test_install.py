@@ -49,11 +49,15 @@ def _fake_hclsm():
         def forward(self, s, m=None):
             return "reference"
 
+    class ED:
+        def forward(self, s):
+            return "reference"
+
     kernels = mod(ssm_scan_fn=f, slot_attention_fn=f, sparse_event_attn_fn=f,
                   ssm_scan_kernel=mod(ssm_scan_fn=f), slot_attention_kernel=mod(slot_attention_fn=f),
                   sparse_event_attn=mod(sparse_event_attn_fn=f))
     dyn = mod(level0_ssm=mod(SimplifiedSSMBlock=Block, Level0SSM=L0), hierarchy_manager=mod(HierarchyManager=HM),
-              level1_event=mod(Level1EventDynamics=L1))
+              level1_event=mod(Level1EventDynamics=L1), event_detector=mod(EventDetector=ED))
     objs = mod(dynamic_slots=mod(DynamicSlotAttention=DSA))
     return mod(kernels=kernels, dynamics=dyn, objects=objs), (Block, DSA, HM, L1)
 
@@ -63,7 +67,7 @@ def test_install_patches_and_uninstall_restores():
     orig = Block.forward
     done = inst.install(pkg)
     done2 = inst.install(pkg)  # idempotent
-    assert done == done2 and len(done) == 13
+    assert done == done2 and len(done) == 14
     assert pkg.kernels.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert pkg.kernels.ssm_scan_kernel.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
     assert Block.forward is not orig
