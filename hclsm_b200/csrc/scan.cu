@@ -1006,9 +1006,15 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
   // B or C of step t in this lane's slot order: pair q holds states
   // 2*(q ^ pq) + {0, 1}
   auto load_bc = [&](const float* base, int t, float2 (&o)[8]) {
-    const float2* row = reinterpret_cast<const float2*>(base + (size_t)t * 16);
+    // pairs 2m and 2m+1 of this lane's slot order are the adjacent pairs of
+    // float4 m ^ (perm >> 2): four 16-byte loads instead of eight 8-byte ones
+    const float4* row = reinterpret_cast<const float4*>(base + (size_t)t * 16);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = row[q ^ pq];
+    for (int m = 0; m < 4; ++m) {
+      const float4 v = row[m ^ (perm >> 2)];
+      o[2 * m] = f2(v.x, v.y);
+      o[2 * m + 1] = f2(v.z, v.w);
+    }
   };
   auto load_ck = [&](int k, float2 (&o)[8], int d) {  // checkpoint before chunk k (k >= 1)
     if (saved) {
