@@ -10,9 +10,12 @@ from .slot_attention_kernel import (  # noqa: F401
 
 from .sparse_event_attn import (  # noqa: F401
     EventTransformer,
+    event_detect,
     sparse_event_attention_fused,
     sparse_event_attn_fn,
 )
+from .level0 import level0_epilogue, level0_forward, masked_mean_pool  # noqa: F401
 
-__all__ = ["sparse_event_attn_fn", "EventTransformer", "sparse_event_attention_fused", "ssm_scan_fn", "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams",
-           "slot_attention_iteration", "slot_attention_iterations"]
+__all__ = ["sparse_event_attn_fn", "EventTransformer", "sparse_event_attention_fused", "event_detect", "ssm_scan_fn",
+           "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration",
+           "slot_attention_iterations", "masked_mean_pool", "level0_epilogue", "level0_forward"]

@@ -20,7 +20,7 @@ import torch
 
 from .. import _lib
 
-__all__ = ["ssm_scan_fn", "ssm_scan", "scan_fwd_raw", "scan_bwd_raw", "bwd_workspace_bytes"]
+__all__ = ["ssm_scan_fn", "ssm_scan", "scan_fwd_raw", "scan_bwd_raw", "bwd_workspace_bytes", "states_bytes"]
 
 
 def _io_dtype(*ts):

@@ -31,4 +31,4 @@ def test_version_and_workspace_query_on_host():
     lib = _lib.load()
     assert lib.hclsm_version() >= 1
     assert lib.hclsm_ssm_scan_bwd_workspace_size(256, 64, 768, 16) > 0
-    assert lib.hclsm_ssm_scan_bwd_workspace_size(2, 16, 32, 128) == 0  # d_state > 16: unsupported
+    assert lib.hclsm_ssm_scan_bwd_workspace_size(2, 16, 32, 128) == 0  # d_state > 64: unsupported
