@@ -1213,15 +1213,13 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         }
         const float2 gyy = f2(gy, gy), dtx = f2(dtxs, dtxs), dvv = f2(dv, dv);
         float2 gB = f2(0.0f, 0.0f), ddA = f2(0.0f, 0.0f);
-        float2 v[16];  // (dB, dC) partials per register slot
+        float2 vB[8], vC[8];  // dB and dC partials per state pair slot
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float2 gs = __ffma2_rn(gyy, Ct[q], gcar[q]);
           gB = __ffma2_rn(gs, Bt[q], gB);
-          const float2 pB = __fmul2_rn(gs, dtx);
-          const float2 pC = __fmul2_rn(gyy, hs[q]);
-          v[2 * q] = f2(pB.x, pC.x);
-          v[2 * q + 1] = f2(pB.y, pC.y);
+          vB[q] = __fmul2_rn(gs, dtx);
+          vC[q] = __fmul2_rn(gyy, hs[q]);
           const float2 w = __fmul2_rn(__half22float2(bits_h2(dwv[q])), gs);
           const float2 R = __fmul2_rn(w, hp[q]);
           ddA = __ffma2_rn(A[q], R, ddA);
@@ -1237,29 +1235,43 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
           static_cast<T*>(p.ddt)[gi] = __float2bfloat16_rn(fmaf(xv, gBs, ddA.x + ddA.y) * mdt);
           if (has_z) static_cast<T*>(p.dz)[gi] = __float2bfloat16_rn(dzv);
         }
-        // reduce (dB, dC) over the warp's 32 channels
+        // reduce dB and dC over the warp's 32 channels.  Pair slot q holds
+        // state pair q ^ pq (pq = lane bits 3, 2): the levels across lane bits
+        // 3 and 2 keep slots [0, n/2) without selects; lane bits 1, 0 and 4
+        // then pick the pair, the element and dB / dC, so that lane l ends
+        // with column l of the slab row (dB of state l for l < 16, else dC of
+        // state l - 16)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fadd2_rn(v[i], shfl2(v[i + 8], 8));
+        for (int i = 0; i < 4; ++i) {
+          vB[i] = __fadd2_rn(vB[i], shfl2(vB[i + 4], 8));
+          vC[i] = __fadd2_rn(vC[i], shfl2(vC[i + 4], 8));
+        }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = __fadd2_rn(v[i], shfl2(v[i + 4], 4));
+        for (int i = 0; i < 2; ++i) {
+          vB[i] = __fadd2_rn(vB[i], shfl2(vB[i + 2], 4));
+          vC[i] = __fadd2_rn(vC[i], shfl2(vC[i + 2], 4));
+        }
         {
           const bool up = (lane & 2) != 0;
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const float2 snd = up ? v[i] : v[i + 2];
-            const float2 kp = up ? v[i + 2] : v[i];
-            v[i] = __fadd2_rn(kp, shfl2(snd, 2));
-          }
+          const float2 sb = up ? vB[0] : vB[1], kb = up ? vB[1] : vB[0];
+          const float2 sc = up ? vC[0] : vC[1], kc = up ? vC[1] : vC[0];
+          vB[0] = __fadd2_rn(kb, shfl2(sb, 2));
+          vC[0] = __fadd2_rn(kc, shfl2(sc, 2));
         }
+        float rB, rC;
         {
           const bool up = (lane & 1) != 0;
-          const float2 snd = up ? v[0] : v[1];
-          const float2 kp = up ? v[1] : v[0];
-          v[0] = __fadd2_rn(kp, shfl2(snd, 1));
+          const float sb = up ? vB[0].x : vB[0].y, kb = up ? vB[0].y : vB[0].x;
+          const float sc = up ? vC[0].x : vC[0].y, kc = up ? vC[0].y : vC[0].x;
+          rB = kb + __shfl_xor_sync(0xffffffffu, sb, 1);
+          rC = kc + __shfl_xor_sync(0xffffffffu, sc, 1);
         }
-        v[0] = __fadd2_rn(v[0], shfl2(v[0], 16));
-        // lane l holds the warp totals of state (l & 15): dB in .x, dC in .y
-        slab[((size_t)warp * K + j) * 32 + lane] = lane < 16 ? v[0].x : v[0].y;
+        float r;
+        {
+          const bool up = (lane & 16) != 0;
+          r = (up ? rC : rB) + __shfl_xor_sync(0xffffffffu, up ? rB : rC, 16);
+        }
+        slab[((size_t)warp * K + j) * 32 + lane] = r;
       }
       __syncthreads();
       {
