@@ -205,6 +205,24 @@ def run_e2e(args, rank, world, dev):
     down = torch.cuda.Stream(dev)  # device -> host (the other PCIe direction)
     comp = torch.cuda.current_stream(dev)
 
+    # chunk boundaries: small chunks first and last, so that the pipeline's
+    # fill (the first upload before any compute) and drain (the last download
+    # after the last compute) are short
+    bounds, s0 = [], 0
+    ramp = [max(1, chunk // 4), max(1, chunk // 2)]
+    sizes = ramp + [chunk] * max(0, (n - 2 * sum(ramp)) // chunk)
+    rest = n - sum(sizes) - sum(ramp)
+    if rest > 0:
+        sizes.append(rest)
+    sizes += ramp[::-1]
+    for sz in sizes:
+        if s0 >= n:
+            break
+        bounds.append((s0, min(n, s0 + sz)))
+        s0 += sz
+    if s0 < n:
+        bounds.append((s0, n))
+
     def step():
         # every host->device copy goes through the upload stream: the copy
         # engine serves copies of one direction in submission order across
@@ -212,8 +230,7 @@ def run_e2e(args, rank, world, dev):
         # all uploads already submitted and stall the compute stream
         with torch.cuda.stream(up):
             A = host["A_log"].to(dev, non_blocking=True)
-        for s0 in range(0, n, chunk):
-            s1 = min(n, s0 + chunk)
+        for s0, s1 in bounds:
             with torch.cuda.stream(up):
                 dv = {k: host[k][s0:s1].to(dev, non_blocking=True) for k in ("x", "dt", "B", "C", "dy")}
                 ready = torch.cuda.Event()
