@@ -164,17 +164,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tile_bytes = (uint32_t)DB * kTok * 128;
   const uint32_t q_bytes = (uint32_t)DB * NP * 128;
 
+  // K of tile ti is fetched as soon as MMA 1 of tile ti - 1 has released the K
+  // buffer (so it overlaps that tile's softmax and MMA 2); V of tile ti once MMA
+  // 2 of tile ti - 1 has released the V buffer
+  auto load_k = [&](int ti) {
+    mbar_expect_tx(&bars[0], tile_bytes + (ti == 0 ? q_bytes : 0));
+    for (int kb = 0; kb < DB; ++kb) {
+      if (ti == 0) tma_load_3d(sQ + (size_t)kb * NP * 128, &mq, kb * 64, 0, f, &bars[0]);
+      tma_load_3d(sK + (size_t)kb * kTok * 128, &mk, kb * 64, ti * kTok, f, &bars[0]);
+    }
+  };
+  auto load_v = [&](int ti) {
+    mbar_expect_tx(&bars[1], tile_bytes);
+    for (int kb = 0; kb < DB; ++kb) tma_load_3d(sV + (size_t)kb * kTok * 128, &mv, kb * 64, ti * kTok, f, &bars[1]);
+  };
+  if (tid == 0) {
+    load_k(0);
+    load_v(0);
+  }
   for (int ti = 0; ti < ntiles; ++ti) {
     const uint32_t par = ti & 1;
-    if (tid == 0) {
-      mbar_expect_tx(&bars[0], tile_bytes + (ti == 0 ? q_bytes : 0));
-      for (int kb = 0; kb < DB; ++kb) {
-        if (ti == 0) tma_load_3d(sQ + (size_t)kb * NP * 128, &mq, kb * 64, 0, f, &bars[0]);
-        tma_load_3d(sK + (size_t)kb * kTok * 128, &mk, kb * 64, ti * kTok, f, &bars[0]);
-      }
-      mbar_expect_tx(&bars[1], tile_bytes);
-      for (int kb = 0; kb < DB; ++kb) tma_load_3d(sV + (size_t)kb * kTok * 128, &mv, kb * 64, ti * kTok, f, &bars[1]);
-    }
     // ---- MMA 1: logits^T = K_tile . Q^T -----------------------------------------------
     wait(0, par);
     if (tid == 0) {
@@ -189,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     wait(2, par);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (tid == 0 && ti + 1 < ntiles) load_k(ti + 1);
     // ---- softmax over the slots of this thread's token ------------------------------
     {
       float lg[NP];
@@ -251,8 +261,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       umma_commit(&bars[3]);
     }
-    wait(3, par);  // K, V and attn buffers are free again
+    wait(3, par);  // the V and attn buffers are free again
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (tid == 0 && ti + 1 < ntiles) load_v(ti + 1);
   }
   // ---- epilogue: row d of out^T -> out[f, :, d] --------------------------------------
   __nv_bfloat16* gO = static_cast<__nv_bfloat16*>(p.out) + (size_t)f * N * D;
