@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -23,6 +24,8 @@ bool set_smem_limit(const void* fn, size_t bytes);
 }  // namespace hclsm
 
 namespace hclsm {
+int event_mha_tc(const void* qkv, const uint8_t* key_pad, void* out, int frames, int T, int H, int HD, float scale,
+                 void* stream);
 namespace event {
 
 // ---- compaction --------------------------------------------------------------------
@@ -525,6 +528,15 @@ extern "C" int hclsm_event_mha(const void* qkv, const uint8_t* key_pad, void* ou
   }
   if (dtype != HCLSM_BF16) return HCLSM_ERR_DTYPE;
   if (reinterpret_cast<uintptr_t>(qkv) % 16 || reinterpret_cast<uintptr_t>(out) % 16) return HCLSM_ERR_ALIGN;
+  // tcgen05 path first (head dim 64, T in {16, 32, 64}); HCLSM_EVENT_MHA=mma
+  // selects the mma.sync kernel below (comparisons, tests)
+  {
+    const char* sel = getenv("HCLSM_EVENT_MHA");
+    if (!(sel && sel[0] == 'm')) {
+      const int rc = event_mha_tc(qkv, key_pad, out, frames, T, H, HD, scale, stream);
+      if (rc != HCLSM_ERR_UNSUPPORTED) return rc;
+    }
+  }
   if (T <= 16) return launch_mha_tp<16>(qkv, key_pad, out, frames, T, H, HD, scale, st);
   if (T <= 32) return launch_mha_tp<32>(qkv, key_pad, out, frames, T, H, HD, scale, st);
   if (T <= 48) return launch_mha_tp<48>(qkv, key_pad, out, frames, T, H, HD, scale, st);

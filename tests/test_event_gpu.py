@@ -185,3 +185,48 @@ def test_gather_scatter_use_the_detector_compaction():
         s1 = scatter(None, states, upd, mask)
         s2 = scatter(None, states, upd, plain)
         assert torch.equal(s1, s2)
+
+
+def _mha_call(qkv, kp, frames, T, H, HD, scale):
+    from hclsm_b200 import _lib
+    out = torch.empty(frames * T, H * HD, dtype=torch.bfloat16, device="cuda")
+    rc = _lib.load().hclsm_event_mha(_lib.ptr(qkv), _lib.ptr(kp), _lib.ptr(out), frames, T, H, HD, scale,
+                                     _lib.dtype_code(torch.bfloat16), _lib.stream_ptr(qkv.device))
+    _lib.check(rc, "hclsm_event_mha")
+    return out
+
+
+@pytest.mark.parametrize("frames,T", [(58, 32), (7, 16), (9, 64), (1, 32), (33, 16)])
+@pytest.mark.parametrize("padded", [False, True])
+def test_event_mha_tcgen05_and_mma_vs_torch(frames, T, padded, monkeypatch):
+    """Both attention kernels (tcgen05 for head dim 64 and T in {16, 32, 64},
+    mma.sync otherwise or when selected) against fp32 torch attention on the
+    same bf16 q|k|v, with dead slots ignored as keys (a frame with every key
+    ignored gives NaN in both, as torch does)."""
+    H, HD = 6, 64
+    E = H * HD
+    g = torch.Generator().manual_seed(frames * T)
+    qkv = torch.randn(frames * T, 3 * E, generator=g).to(torch.bfloat16).cuda()
+    kp = None
+    if padded:
+        kp = (torch.rand(frames, T, generator=g) < 0.3).to(torch.uint8)
+        if frames > 1:
+            kp[0] = 1  # a frame whose keys are all ignored
+        kp = kp.cuda()
+    scale = HD ** -0.5
+    q, k, v = (qkv.float().reshape(frames, T, 3, H, HD)[:, :, i].transpose(1, 2) for i in range(3))
+    logits = (q @ k.transpose(-1, -2)) * scale
+    if kp is not None:
+        logits = logits.masked_fill(kp.bool()[:, None, None, :], float("-inf"))
+    ref = (torch.softmax(logits, dim=-1) @ v).transpose(1, 2).reshape(frames * T, E)
+    outs = {}
+    for sel in ("tc", "mma"):
+        if sel == "mma":
+            monkeypatch.setenv("HCLSM_EVENT_MHA", "mma")
+        else:
+            monkeypatch.delenv("HCLSM_EVENT_MHA", raising=False)
+        outs[sel] = _mha_call(qkv, kp, frames, T, H, HD, scale).float()
+    for sel, o in outs.items():
+        nan_ref = torch.isnan(ref)
+        assert torch.equal(torch.isnan(o), nan_ref), sel
+        assert rel_err(o[~nan_ref].cpu().numpy(), ref[~nan_ref].cpu().numpy()) < 2e-2, sel
