@@ -831,6 +831,12 @@ __device__ __forceinline__ void tmem_ld8_nc(uint32_t taddr, float (&v)[8]) {
                : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
                : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_wait_ld_tied16(float (&a)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]), "+f"(a[5]), "+f"(a[6]), "+f"(a[7]),
+                 "+f"(a[8]), "+f"(a[9]), "+f"(a[10]), "+f"(a[11]), "+f"(a[12]), "+f"(a[13]), "+f"(a[14]),
+                 "+f"(a[15]));
+}
 __device__ __forceinline__ void tmem_wait_ld_tied(float (&a)[16], float (&b)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]), "+f"(a[5]), "+f"(a[6]), "+f"(a[7]),
@@ -862,7 +868,11 @@ constexpr int kW16Threads = 256;
 constexpr int kW16Ch = 256;   // channels per group
 constexpr int kW16K = 10;     // history steps per chunk
 static_assert(kW16K == kStateEvery, "the forward's snapshots are the packed kernel's chunk boundaries");
-constexpr int kW16Cols = 24;  // TMEM columns per step: 16 x h (f32) + 8 x dA (f16x2)
+// TMEM columns of a thread: h slots 0..K (16 fp32 each; slot 0 holds the
+// chunk's starting state, slot j + 1 the state after step j), then the K
+// steps' dA as f16 pairs (8 columns each)
+constexpr int kW16DACol = 16 * (kW16K + 1);
+static_assert(kW16DACol + 8 * kW16K <= 256, "a warp pair shares 512 TMEM columns");
 constexpr int kW16MaxSlots = 1024;
 
 struct W16Smem {
@@ -960,6 +970,11 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
       sCf[i] = s < S ? __bfloat162float(Cm[(int64_t)t * S + s]) : 0.0f;
     }
   }
+  {  // zero the tiles: the columns past a partial group's channels are never copied
+    float4* z4 = reinterpret_cast<float4*>(tiles);
+    for (int e = tid; e < (int)(Sm::tiles_bytes() / 16); e += kW16Threads) z4[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the bulk copies overwrite them
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -969,7 +984,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
   const int n_items = (g_end - g_begin) * items_per_group;
   auto issue = [&](int it) {
     if (it >= n_items) return;
-    const int g = g_begin + it / items_per_group;
+    const int g = g_end - 1 - it / items_per_group;  // groups run last to first
     const int r = it % items_per_group;
     const bool rev = saved || r >= nck;
     const int k = rev ? (items_per_group - 1 - r) : r;
@@ -1045,7 +1060,9 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
   };
 
   int it = 0;
-  for (int g = g_begin; g < g_end; ++g) {
+  // groups run last to first: only the last group of the channels can be
+  // partial, and it then runs on tiles whose unused columns are still zero
+  for (int g = g_end - 1; g >= g_begin; --g) {
     const int d = g * kW16Ch + tid;
     const bool act = d < D;
     float2 A[8];
@@ -1130,11 +1147,18 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
 #pragma unroll
         for (int q = 0; q < 8; ++q) hnext[q] = f2(0.0f, 0.0f);
       }
-      // recompute the chunk: h_t (fp32) and dA_t (f16 pairs) into TMEM
+      // recompute the chunk: the starting state into h slot 0, then h_t (fp32,
+      // slot j + 1) and dA_t (f16 pairs) of every step into TMEM
+      {
+        float hv[16];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { hv[2 * q] = hs[q].x; hv[2 * q + 1] = hs[q].y; }
+        tmem_st16(tmem, hv);
+      }
 #pragma unroll 2
       for (int j = 0; j < n; ++j) {
-        const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
-        float dv = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
+        const float xv = __bfloat162float(st[(size_t)j * kW16Ch]);
+        float dv = __bfloat162float(st[TILE + (size_t)j * kW16Ch]);
         if (SOFTPLUS) dv = softplus_f(dv);
         if (CLAMP) dv = fminf(fmaxf(dv, 1e-3f), 1.0f);
         const float2 dtx = f2(dv * xv, dv * xv);
@@ -1152,40 +1176,34 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
           hv[2 * q + 1] = hs[q].y;
           dw[q] = __uint_as_float(h2_bits(e));
         }
-        const uint32_t col = tmem + (uint32_t)(j * kW16Cols);
-        tmem_st16(col, hv);
-        tmem_st8(col + 16, dw);
+        tmem_st16(tmem + (uint32_t)(16 * (j + 1)), hv);
+        tmem_st8(tmem + (uint32_t)(kW16DACol + 8 * j), dw);
       }
       tmem_wait_st();
-      float nh[16], nd[8];
-      {
-        const uint32_t col = tmem + (uint32_t)((n - 1) * kW16Cols);
-        tmem_ld8_nc(col + 16, nd);
-        if (n - 1 > 0) tmem_ld16_nc(col - kW16Cols, nh);
-      }
-#pragma unroll 2
-      for (int j = n - 1; j >= 0; --j) {
+
+      // reverse walk.  Step j reads h slots j + 1 (h_t) and j (h_{t-1}) and
+      // dA_j; three h buffers rotate so that the prefetch of slot j - 1 lands
+      // in the buffer step j + 1 finished with, and no registers are copied.
+      float H0[16], H1[16], H2[16], Dc[8];
+      tmem_ld16_nc(tmem + (uint32_t)(16 * n), H0);
+      tmem_ld16_nc(tmem + (uint32_t)(16 * (n - 1)), H1);
+      tmem_ld8_nc(tmem + (uint32_t)(kW16DACol + 8 * (n - 1)), Dc);
+      tmem_wait_ld_tied16(H0);
+      auto step = [&](const int j, float (&Hs)[16], float (&Hp)[16], float (&Hn)[16]) {
         const int t = t0 + j;
-        tmem_wait_ld_tied(nh, nd);
-        float2 hp[8];
-        uint32_t dwv[8];
+        tmem_wait_ld_tied(Hp, Dc);
+        float2 dA[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dA[q] = __half22float2(bits_h2(__float_as_uint(Dc[q])));
         if (j > 0) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) hp[q] = f2(nh[2 * q], nh[2 * q + 1]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) hp[q] = hk[q];
+          tmem_ld8_nc(tmem + (uint32_t)(kW16DACol + 8 * (j - 1)), Dc);
+          tmem_ld16_nc(tmem + (uint32_t)(16 * (j - 1)), Hn);
         }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) dwv[q] = __float_as_uint(nd[q]);
-        if (j > 0) {
-          const uint32_t col = tmem + (uint32_t)((j - 1) * kW16Cols);
-          tmem_ld8_nc(col + 16, nd);
-          if (j - 1 > 0) tmem_ld16_nc(col - kW16Cols, nh);
-        }
-        const float xv = act ? __bfloat162float(st[(size_t)j * kW16Ch]) : 0.0f;
-        const float draw = act ? __bfloat162float(st[TILE + (size_t)j * kW16Ch]) : 0.0f;
-        float gy = act ? __bfloat162float(st[2 * TILE + (size_t)j * kW16Ch]) : 0.0f;
+        // tile columns past the group's channels stay zero, so an inactive
+        // lane computes zeros without selects (its stores are skipped)
+        const float xv = __bfloat162float(st[(size_t)j * kW16Ch]);
+        const float draw = __bfloat162float(st[TILE + (size_t)j * kW16Ch]);
+        float gy = __bfloat162float(st[2 * TILE + (size_t)j * kW16Ch]);
         // dv = clamp(softplus(raw)); mdt = d dv / d raw
         float dv = draw, mdt = 1.0f;
         if (SOFTPLUS) {
@@ -1202,10 +1220,10 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         load_bc(sCf, t, Ct);
         float dzv = 0.0f;
         if (has_z) {
-          const float zv = act ? __bfloat162float(st[3 * TILE + (size_t)j * kW16Ch]) : 0.0f;
+          const float zv = __bfloat162float(st[3 * TILE + (size_t)j * kW16Ch]);
           float2 ys2 = f2(0.0f, 0.0f);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) ys2 = __ffma2_rn(hs[q], Ct[q], ys2);
+          for (int q = 0; q < 8; ++q) ys2 = __ffma2_rn(f2(Hs[2 * q], Hs[2 * q + 1]), Ct[q], ys2);
           const float ys = fmaf(Dd, xv, ys2.x + ys2.y);
           const float sg = sigmoid(zv);
           dzv = gy * ys * sg * (1.0f + zv * (1.0f - sg));
@@ -1216,16 +1234,16 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         float2 vB[8], vC[8];  // dB and dC partials per state pair slot
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
+          const float2 hp = f2(Hp[2 * q], Hp[2 * q + 1]);
           const float2 gs = __ffma2_rn(gyy, Ct[q], gcar[q]);
           gB = __ffma2_rn(gs, Bt[q], gB);
           vB[q] = __fmul2_rn(gs, dtx);
-          vC[q] = __fmul2_rn(gyy, hs[q]);
-          const float2 w = __fmul2_rn(__half22float2(bits_h2(dwv[q])), gs);
-          const float2 R = __fmul2_rn(w, hp[q]);
+          vC[q] = __fmul2_rn(gyy, f2(Hs[2 * q], Hs[2 * q + 1]));
+          const float2 w = __fmul2_rn(dA[q], gs);
+          const float2 R = __fmul2_rn(w, hp);
           ddA = __ffma2_rn(A[q], R, ddA);
           gAcc[q] = __ffma2_rn(dvv, R, gAcc[q]);
           gcar[q] = w;
-          hs[q] = hp[q];
         }
         dDacc = fmaf(gy, xv, dDacc);
         if (act) {
@@ -1272,10 +1290,18 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
           r = (up ? rC : rB) + __shfl_xor_sync(0xffffffffu, up ? rB : rC, 16);
         }
         slab[((size_t)warp * K + j) * 32 + lane] = r;
+      };
+      for (int j = n - 1;;) {
+        step(j, H0, H1, H2);
+        if (--j < 0) break;
+        step(j, H1, H2, H0);
+        if (--j < 0) break;
+        step(j, H2, H0, H1);
+        if (--j < 0) break;
       }
       __syncthreads();
       {
-        const bool first = (g == g_begin);
+        const bool first = (g == g_end - 1);
         for (int e = tid; e < n * 32; e += kW16Threads) {
           const int j = e >> 5, vv = e & 31;
           float acc = 0.0f;
