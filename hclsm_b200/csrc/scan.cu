@@ -899,7 +899,15 @@ __device__ __forceinline__ float2 shfl2(float2 v, int m) {
   return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-template <bool CLAMP, bool SOFTPLUS>
+// bf16 store that only predicated-on lanes execute (no branch, so the step
+// stays one scheduling region)
+__device__ __forceinline__ void st_bf16_if(__nv_bfloat16* ptr, float v, bool pred) {
+  const unsigned short u = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  asm volatile("{ .reg .pred q; setp.ne.b32 q, %2, 0; @q st.global.b16 [%0], %1; }" ::"l"(ptr), "h"(u),
+               "r"((int)pred));
+}
+
+template <bool CLAMP, bool SOFTPLUS, bool HASZ>
 __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams p) {
   using T = __nv_bfloat16;
   using Sm = W16Smem;
@@ -945,7 +953,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
   const T* __restrict__ gdt = static_cast<const T*>(p.dt);
   const T* __restrict__ gdy = static_cast<const T*>(p.dy);
   const T* __restrict__ gz = static_cast<const T*>(p.z);
-  const bool has_z = p.z != nullptr;
+  constexpr bool has_z = HASZ;
   const bool has_D = p.Dp != nullptr;
 
   if (warp == 0) {
@@ -1195,9 +1203,10 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         float2 dA[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) dA[q] = __half22float2(bits_h2(__float_as_uint(Dc[q])));
-        if (j > 0) {
-          tmem_ld8_nc(tmem + (uint32_t)(kW16DACol + 8 * (j - 1)), Dc);
-          tmem_ld16_nc(tmem + (uint32_t)(16 * (j - 1)), Hn);
+        {  // prefetch for step j - 1 (at j = 0 a harmless reload of slot 0)
+          const int jn = j > 0 ? j - 1 : 0;
+          tmem_ld8_nc(tmem + (uint32_t)(kW16DACol + 8 * jn), Dc);
+          tmem_ld16_nc(tmem + (uint32_t)(16 * jn), Hn);
         }
         // tile columns past the group's channels stay zero, so an inactive
         // lane computes zeros without selects (its stores are skipped)
@@ -1219,7 +1228,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         load_bc(sBf, t, Bt);
         load_bc(sCf, t, Ct);
         float dzv = 0.0f;
-        if (has_z) {
+        if constexpr (HASZ) {
           const float zv = __bfloat162float(st[3 * TILE + (size_t)j * kW16Ch]);
           float2 ys2 = f2(0.0f, 0.0f);
 #pragma unroll
@@ -1246,12 +1255,12 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
           gcar[q] = w;
         }
         dDacc = fmaf(gy, xv, dDacc);
-        if (act) {
+        {
           const int64_t gi = (b * L + t) * (int64_t)D + d;
           const float gBs = gB.x + gB.y;
-          static_cast<T*>(p.dx)[gi] = __float2bfloat16_rn(fmaf(dv, gBs, Dd * gy));
-          static_cast<T*>(p.ddt)[gi] = __float2bfloat16_rn(fmaf(xv, gBs, ddA.x + ddA.y) * mdt);
-          if (has_z) static_cast<T*>(p.dz)[gi] = __float2bfloat16_rn(dzv);
+          st_bf16_if(static_cast<T*>(p.dx) + gi, fmaf(dv, gBs, Dd * gy), act);
+          st_bf16_if(static_cast<T*>(p.ddt) + gi, fmaf(xv, gBs, ddA.x + ddA.y) * mdt, act);
+          if constexpr (HASZ) st_bf16_if(static_cast<T*>(p.dz) + gi, dzv, act);
         }
         // reduce dB and dC over the warp's 32 channels.  Pair slot q holds
         // state pair q ^ pq (pq = lane bits 3, 2): the levels across lane bits
@@ -1291,13 +1300,16 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         }
         slab[((size_t)warp * K + j) * 32 + lane] = r;
       };
-      for (int j = n - 1;;) {
+      // blocks of three steps without branches between them, then the rest
+      int j = n - 1;
+      for (; j >= 2; j -= 3) {
         step(j, H0, H1, H2);
-        if (--j < 0) break;
-        step(j, H1, H2, H0);
-        if (--j < 0) break;
-        step(j, H2, H0, H1);
-        if (--j < 0) break;
+        step(j - 1, H1, H2, H0);
+        step(j - 2, H2, H0, H1);
+      }
+      if (j >= 0) {
+        step(j, H0, H1, H2);
+        if (j >= 1) step(j - 1, H1, H2, H0);
       }
       __syncthreads();
       {
@@ -1548,7 +1560,7 @@ static int launch_bwd_t(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) 
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
 }
 
-template <bool CLAMP, bool SOFTPLUS>
+template <bool CLAMP, bool SOFTPLUS, bool HASZ>
 static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t st) {
   const size_t smem = W16Smem::total(p.L);
   if (smem > 227 * 1024) return HCLSM_ERR_UNSUPPORTED;
@@ -1557,7 +1569,7 @@ static int launch_bwd_bf16(const BwdParams& p, const BwdPlan& pl, cudaStream_t s
   q.groups = (p.D + kW16Ch - 1) / kW16Ch;
   // the channel split of the plan counts 128-channel groups; keep its CTA count
   q.groups_per_cta = (q.groups + pl.nsplit - 1) / pl.nsplit;
-  auto fn = scan_bwd_bf16_kernel<CLAMP, SOFTPLUS>;
+  auto fn = scan_bwd_bf16_kernel<CLAMP, SOFTPLUS, HASZ>;
   if (!set_smem_limit(reinterpret_cast<const void*>(fn), smem)) return HCLSM_ERR_LAUNCH;
   fn<<<dim3((unsigned)p.nseq, pl.nsplit), kW16Threads, smem, st>>>(q);
   return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
@@ -1569,9 +1581,15 @@ static int launch_bwd(const BwdParams& p, const BwdPlan& pl, bool clamp, cudaStr
     // the packed kernel keeps B, C and dB|dC of the whole sequence in shared
     // memory; longer sequences take the generic kernel
     if (pl.SP == 16 && W16Smem::total(p.L) <= 227 * 1024) {
+      if (p.z) {
+        if (p.softplus)
+          return clamp ? launch_bwd_bf16<true, true, true>(p, pl, st) : launch_bwd_bf16<false, true, true>(p, pl, st);
+        return clamp ? launch_bwd_bf16<true, false, true>(p, pl, st) : launch_bwd_bf16<false, false, true>(p, pl, st);
+      }
       if (p.softplus)
-        return clamp ? launch_bwd_bf16<true, true>(p, pl, st) : launch_bwd_bf16<false, true>(p, pl, st);
-      return clamp ? launch_bwd_bf16<true, false>(p, pl, st) : launch_bwd_bf16<false, false>(p, pl, st);
+        return clamp ? launch_bwd_bf16<true, true, false>(p, pl, st) : launch_bwd_bf16<false, true, false>(p, pl, st);
+      return clamp ? launch_bwd_bf16<true, false, false>(p, pl, st)
+                   : launch_bwd_bf16<false, false, false>(p, pl, st);
     }
   }
   if (p.states) return HCLSM_ERR_UNSUPPORTED;  // only the packed kernel reads snapshots
