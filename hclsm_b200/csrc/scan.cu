@@ -1163,8 +1163,7 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         for (int q = 0; q < 8; ++q) { hv[2 * q] = hs[q].x; hv[2 * q + 1] = hs[q].y; }
         tmem_st16(tmem, hv);
       }
-#pragma unroll 2
-      for (int j = 0; j < n; ++j) {
+      auto rstep = [&](const int j) {
         const float xv = __bfloat162float(st[(size_t)j * kW16Ch]);
         float dv = __bfloat162float(st[TILE + (size_t)j * kW16Ch]);
         if (SOFTPLUS) dv = softplus_f(dv);
@@ -1186,6 +1185,16 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         }
         tmem_st16(tmem + (uint32_t)(16 * (j + 1)), hv);
         tmem_st8(tmem + (uint32_t)(kW16DACol + 8 * j), dw);
+      };
+      // full chunks (all but possibly the last) written out with constant step
+      // indices, in the variants where that fits the register file
+      constexpr bool kUnrollChunk = SOFTPLUS || (!CLAMP && !HASZ);
+      if (kUnrollChunk && n == K) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) rstep(j);
+      } else {
+#pragma unroll 2
+        for (int j = 0; j < n; ++j) rstep(j);
       }
       tmem_wait_st();
 
@@ -1300,16 +1309,29 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         }
         slab[((size_t)warp * K + j) * 32 + lane] = r;
       };
-      // blocks of three steps without branches between them, then the rest
-      int j = n - 1;
-      for (; j >= 2; j -= 3) {
-        step(j, H0, H1, H2);
-        step(j - 1, H1, H2, H0);
-        step(j - 2, H2, H0, H1);
-      }
-      if (j >= 0) {
-        step(j, H0, H1, H2);
-        if (j >= 1) step(j - 1, H1, H2, H0);
+      static_assert(K == 10, "the full-chunk walk below is written out for 10 steps");
+      if (kUnrollChunk && n == K) {
+        step(9, H0, H1, H2);
+        step(8, H1, H2, H0);
+        step(7, H2, H0, H1);
+        step(6, H0, H1, H2);
+        step(5, H1, H2, H0);
+        step(4, H2, H0, H1);
+        step(3, H0, H1, H2);
+        step(2, H1, H2, H0);
+        step(1, H2, H0, H1);
+        step(0, H0, H1, H2);
+      } else {  // blocks of three steps without branches between them, then the rest
+        int j = n - 1;
+        for (; j >= 2; j -= 3) {
+          step(j, H0, H1, H2);
+          step(j - 1, H1, H2, H0);
+          step(j - 2, H2, H0, H1);
+        }
+        if (j >= 0) {
+          step(j, H0, H1, H2);
+          if (j >= 1) step(j - 1, H1, H2, H0);
+        }
       }
       __syncthreads();
       {
