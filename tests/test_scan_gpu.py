@@ -127,6 +127,29 @@ def test_config4_slice():
         assert rel_err(_np(got), gr[name]) < 2e-2, name
 
 
+@pytest.mark.parametrize("gated", [False, True])
+def test_partial_group_in_multi_group_cta(gated):
+    """148 sequences (one per SM) put every channel group of a sequence into one
+    CTA of the packed backward; d_inner=1000 makes the last of its four groups
+    232 channels wide, and L=23 ends on a 3-step chunk.  Both backward paths
+    (forward snapshots and forward sweep) against the oracle."""
+    from hclsm_b200.kernels.ssm_scan_kernel import states_bytes
+    nseq, L, Dn, S = 148, 23, 1000, 16
+    d = scan_inputs(nseq, L, Dn, S, dtype=torch.bfloat16, seed=9, device="cuda", gated=gated)
+    o = _oracle_inputs(d)
+    D, z = d.get("D"), d.get("z")
+    st = torch.empty(states_bytes(nseq, L, Dn, S, torch.bfloat16), dtype=torch.uint8, device="cuda")
+    y = scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], D, z, states=st)
+    yr = oscan.scan_fwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o.get("D"), o.get("z"))
+    assert rel_err(_np(y), yr) < 2e-2
+    gr = oscan.scan_bwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o["dy"], o.get("D"), o.get("z"))
+    for states in (st, None):
+        grads = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], D, z, states=states)
+        for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), grads):
+            if got is not None:
+                assert rel_err(_np(got), gr[name]) < 2e-2, (name, states is None)
+
+
 def test_deterministic_and_no_device_error():
     d = scan_inputs(16, 64, 256, 16, dtype=torch.bfloat16, seed=3, device="cuda")
     a = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"])
