@@ -194,8 +194,12 @@ __device__ __forceinline__ uint32_t f2_to_bf2(float a, float b) {
 
 template <int SP, bool CLAMP>
 __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams p) {
-  __shared__ float2 sB[kFwdTC][SP];
-  __shared__ float2 sC[kFwdTC][SP];
+  // B and C of a 64-step window, one float per state: a 16-byte load brings
+  // four states, and each is paired with itself in registers for the packed
+  // math (half the shared loads of storing the pairs; the MIO queue that the
+  // loads share with the exponentials is this kernel's bound)
+  __shared__ __align__(16) float sB[kFwdTC][SP];
+  __shared__ __align__(16) float sC[kFwdTC][SP];
 
   const int64_t b = blockIdx.y;
   const int D = p.D, S = p.S, L = p.L;
@@ -258,8 +262,8 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
       const int64_t r = (row0 + t0 + tt) * S;
       const float bv = s < S ? __bfloat162float(Bm[r + s]) : 0.0f;
       const float cv = s < S ? __bfloat162float(Cm[r + s]) : 0.0f;
-      sB[tt][s] = make_float2(bv, bv);
-      sC[tt][s] = make_float2(cv, cv);
+      sB[tt][s] = bv;
+      sC[tt][s] = cv;
     }
     __syncthreads();
     for (int tb = 0; tb < tc; tb += kFwdBlk) {
@@ -285,8 +289,9 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
           for (int s = 0; s < SP; ++s) {
             const float2 ar = __fmul2_rn(dv, A2[s]);
             const float2 dA = make_float2(ex2(ar.x), ex2(ar.y));
-            h[s] = __ffma2_rn(dA, h[s], __fmul2_rn(dtx, sB[tt][s]));
-            acc = __ffma2_rn(h[s], sC[tt][s], acc);
+            const float bb = sB[tt][s], cc = sC[tt][s];
+            h[s] = __ffma2_rn(dA, h[s], __fmul2_rn(dtx, make_float2(bb, bb)));
+            acc = __ffma2_rn(h[s], make_float2(cc, cc), acc);
           }
           acc = __ffma2_rn(Dv, xv, acc);
           if (has_z) {
