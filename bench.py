@@ -1,12 +1,18 @@
-"""Benchmark of the HCLSM hot path on B200: selective-scan forward+backward at
-BASELINE config 4 (per GPU: 8192 sequences = 64 videos x 128 slots, L=256,
-d_inner=2048, d_state=16, bf16 I/O, fp32 state).
+"""Benchmark of the HCLSM hot path on B200.
+
+Headline: the selective-scan forward + backward of BASELINE config 4, strong
+scaled: one job of 64 videos x 128 slots = 8192 sequences (L=256, d_inner=2048,
+d_state=16, bf16 I/O, fp32 state), rank r of N scanning sequences
+[r * 8192 / N, (r + 1) * 8192 / N).  Beside it, legs for configs 0-3 (the
+fp32 scan latency, the config-1 scan fwd+bwd, slot attention, sparse event
+attention), each with its roofline and a CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N>1 runs under torchrun, one process per GPU; every rank scans its own 8192
-sequences (sequences are independent: no collective on the data path) and the
-whole-job throughput is total sequences / max-over-ranks device time.
+N>1 runs under torchrun, one process per GPU over NCCL.  The scan needs no
+collective on its data path (sequences are independent); after the timed
+region NCCL all-gathers every rank's outputs to rank 0, which checks them bit
+for bit against its own run of the same sequences, and all-reduces dA_log.
 
 Output: one JSON line on rank 0.
 """
@@ -25,7 +31,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L, DI, DS = 256, 2048, 16
-SEQS_PER_GPU = 8192
+GLOBAL_SEQS = 8192
+SEED = 4242
 # Algorithmic bytes per sequence (bf16 I/O).  Forward reads x, dt, B, C and
 # writes y; backward reads x, dt, dy, B, C and writes dx, ddt, dB, dC.  A_log
 # (read) and dA_log (written), fp32, are counted once per call.
@@ -33,11 +40,19 @@ FWD_BYTES_PER_SEQ = 3 * L * DI * 2 + 2 * L * DS * 2
 BWD_BYTES_PER_SEQ = 5 * L * DI * 2 + 4 * L * DS * 2
 ALOG_BYTES = DI * DS * 4
 # DRAM bytes per sequence of the backward kernel measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum, 148-sequence config-4 slice
-# on the state-snapshot path; see profiles/scan_config4_slice_ncu.md).  Above
-# the algorithmic bytes by the forward's snapshots that the backward reads
-# (3.28 MB per sequence).
+# (dram__bytes_read.sum + dram__bytes_write.sum on a 148-sequence config-4
+# slice of the state-snapshot path); the forward's snapshots that the backward
+# reads (3.28 MB per sequence) put it above the algorithmic bytes.
 BWD_TRAFFIC_PER_SEQ = 8.33e6
+# exponentials per (t, channel, state) element: one in the forward, one in the
+# backward's recomputation
+EXPS_PER_ELEM_STEP = 2
+# config 2: FLOP per frame (QK^T, attn V, W_q, GRU, MLP over 3 iterations, plus
+# the k/v projections) and config 3: FLOP per event frame (3 layers of qkv,
+# attention, out-proj, SwiGLU, plus proj_in / proj_out) at 32 slots, dim 384
+SLOT_FLOP_PER_FRAME = 7.29e10 / 128
+EVENT_FLOP_PER_FRAME = 2 * 32 * (384 * 384 * 2 + 3 * (384 * 3 * 384 + 384 * 384 + 3 * 384 * 1536)) + \
+    3 * 2 * 2 * 6 * 32 * 32 * 64
 
 
 def parse():
@@ -46,19 +61,70 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU, help="sequences per GPU")
-    ap.add_argument("--e2e-seqs", type=int, default=1024, help="sequences per rank in the end-to-end leg")
-    ap.add_argument("--e2e-chunk", type=int, default=128, help="sequences per pipelined copy/compute chunk")
-    ap.add_argument("--ref-seqs", type=int, default=16, help="sequences per CPU-baseline step")
+    ap.add_argument("--seqs", type=int, default=GLOBAL_SEQS, help="global sequences of the config-4 job")
+    ap.add_argument("--ref-seqs", type=int, default=4, help="config-4 sequences per CPU-baseline step")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-extra", action="store_true", help="skip the slot / event attention legs")
+    ap.add_argument("--no-verify", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config 0-3 legs")
     return ap.parse_args()
 
 
-def cpu_reference(nseq, steps, warmup):
-    """Time the CPU restatement of the reference scan (fwd + bwd) on a bounded
-    sample of the config-4 workload, using every host core."""
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def _best_of(fn, reps=3, warm=1):
+    for _ in range(warm):
+        fn()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return min(ts)
+
+
+# ---- CPU baselines: the reference's own CPU path (PyTorch), restated --------------
+def cpu_scan(nseq, L_, d, s, bwd, dtype_name, reps=3, seed=1234, gated=False, clamp_ref=True):
+    """sequential_ssm_scan (+ autograd) of the reference, restated op for op in
+    PyTorch on the host cores, on ``nseq`` sequences.  Returns seconds per call."""
+    import torch
+    import torch.nn.functional as F
+
+    from hclsm_b200.workloads import scan_inputs
+    from oracle import torch_ref
+
+    torch.set_num_threads(_cpu_threads())
+    d_ = scan_inputs(nseq, L_, d, s, dtype=getattr(torch, dtype_name), seed=seed, gated=gated)
+    f = {k: v.float() for k, v in d_.items()}
+
+    def run():
+        leaves = {k: f[k].clone().requires_grad_(bwd) for k in ("x", "dt", "A_log", "B", "C")}
+        y = torch_ref.sequential_ssm_scan(leaves["x"], leaves["dt"], leaves["A_log"], leaves["B"], leaves["C"])
+        if gated:
+            y = (y + f["D"] * leaves["x"]) * F.silu(f["z"])
+        if bwd:
+            y.backward(f["dy"])
+
+    return _best_of(run, reps=reps)
+
+
+def cpu_scan_c(nseq, reps=1):
+    """The C restatement of the scan (fwd + bwd), all host cores, on nseq
+    config-4 sequences.  Returns (seconds per call, threads)."""
     import torch
 
     from hclsm_b200.workloads import scan_inputs
@@ -68,19 +134,57 @@ def cpu_reference(nseq, steps, warmup):
     d = scan_inputs(nseq, L, DI, DS, dtype=torch.bfloat16, seed=1234)
     o = {k: v.float().numpy() for k, v in d.items()}
 
-    def step():
+    def run():
         oscan.scan_fwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], threads=threads)
         oscan.scan_bwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o["dy"], threads=threads)
 
-    for _ in range(warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        step()
-    dt = time.perf_counter() - t0
-    return nseq * steps / dt, threads, dt / steps
+    return _best_of(run, reps=reps), threads
 
 
+def cpu_slot(reps=3):
+    """Config 2 on the host: k/v projections + 3 x _iteration_step, fp32."""
+    import torch
+    import torch.nn.functional as F
+
+    from hclsm_b200.workloads import slot_inputs
+    from oracle import torch_ref
+
+    torch.set_num_threads(_cpu_threads())
+    d = slot_inputs(seed=0)
+    W = d["weights"]
+
+    def run():
+        with torch.no_grad():
+            k = F.linear(d["inputs"], W["project_k.weight"])
+            v = F.linear(d["inputs"], W["project_v.weight"])
+            s = d["slots"]
+            for _ in range(3):
+                s = torch_ref.iteration_step(s, k, v, W)
+
+    return _best_of(run, reps=reps)
+
+
+def cpu_event(reps=3):
+    """Config 3 on the host: naive_sparse_event_attention with the 3-layer
+    Level-1 transformer, fp32.  Returns (seconds per call, event frames)."""
+    import torch
+
+    from hclsm_b200.workloads import event_inputs
+    from oracle import torch_ref
+
+    torch.set_num_threads(_cpu_threads())
+    e = event_inputs(seed=20)
+    W = e["weights"]
+
+    def run():
+        with torch.no_grad():
+            torch_ref.naive_sparse_event_attention(
+                e["states"], e["mask"], lambda fr: torch_ref.level1_event(fr, W, e["heads"], e["layers"]))
+
+    return _best_of(run, reps=reps), int(e["mask"].sum().item())
+
+
+# ---- clocks ----------------------------------------------------------------------
 class Clocks:
     """nvidia-smi sampler running during the timed region."""
 
@@ -120,108 +224,208 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def run_b200(args, rank, world, local_rank):
+def _max_over_ranks(vals, dev, world):
     import torch
     import torch.distributed as dist
 
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _barrier(world):
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+
+
+# ---- config 4: the headline ----------------------------------------------------------
+def run_config4(args, rank, world, dev):
+    import torch
+
     import hclsm_b200
     from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, scan_bwd_raw, scan_fwd_raw, states_bytes
-    from hclsm_b200.workloads import scan_inputs
+    from hclsm_b200.shard import shard_range
+    from hclsm_b200.workloads import scan_inputs_range
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    nseq = args.seqs
-    d = scan_inputs(nseq, L, DI, DS, dtype=torch.bfloat16, seed=1000 + rank, device=dev)
+    s0, s1 = shard_range(args.seqs // 64, rank, world)
+    s0, s1 = s0 * 64, s1 * 64
+    nseq = s1 - s0
+    d = scan_inputs_range(s0, nseq, L, DI, DS, dtype=torch.bfloat16, seed=SEED, device=dev)
     ws = torch.empty(bwd_workspace_bytes(nseq, L, DI, DS), dtype=torch.uint8, device=dev)
-    # the forward keeps h every 10 steps; the backward starts from those snapshots
     st = torch.empty(states_bytes(nseq, L, DI, DS, torch.bfloat16), dtype=torch.uint8, device=dev)
     y = torch.empty_like(d["x"])
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def fwd():
         scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y, states=st)
+
+    def bwd():
         return scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws, states=st)
 
     for _ in range(args.warmup):
-        g = step()
+        fwd()
+        g = bwd()
     del g
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    clocks = Clocks(local_rank) if rank == 0 else None
+    _barrier(world)
+    clocks = Clocks(dev.index) if rank == 0 else None
     if clocks:
         time.sleep(0.3)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     ev[0].record(stream)
     for i in range(args.steps):
-        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y, states=st)
+        fwd()
         ev[2 * i + 1].record(stream)
-        g = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws, states=st)
+        g = bwd()
         ev[2 * i + 2].record(stream)
         del g
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     clk = clocks.stop() if clocks else None
     total_ms = ev[0].elapsed_time(ev[2 * args.steps])
     fwd_ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps
     bwd_ms = sum(ev[2 * i + 1].elapsed_time(ev[2 * i + 2]) for i in range(args.steps)) / args.steps
-    t = torch.tensor([total_ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, fwd_ms, bwd_ms = t.tolist()
+    total_ms, fwd_ms, bwd_ms = _max_over_ranks([total_ms, fwd_ms, bwd_ms], dev, world)
     err = hclsm_b200.device_error()
     if err:
         raise RuntimeError(f"device error {err}")
+    res = dict(ms_per_step=total_ms / args.steps, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk, seqs_per_rank=nseq)
+    if not args.no_verify:
+        fwd()
+        grads = bwd()
+        res["verify"] = verify_config4(args, rank, world, dev, (s0, s1), y, grads, d)
+        del grads
     del d, ws, y, st
     torch.cuda.empty_cache()
-    e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)
-    return dict(ms_per_step=total_ms / args.steps, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk, e2e=e2e)
+    return res
 
 
-def run_e2e(args, rank, world, dev):
-    """Inputs in pinned host memory; per step: H2D copy, forward + backward via
-    ``ssm_scan_fn`` and autograd, D2H copy of y and every gradient.  Chunks of
-    sequences are pipelined over an upload stream, the compute stream and a
-    download stream, so both PCIe directions run at once."""
+def verify_config4(args, rank, world, dev, shard, y, grads, d):
+    """Outside the timed region.  N > 1: NCCL all-gathers y, dx, ddt, dB, dC of
+    every rank in rounds of 64 sequences per rank and all-reduces dA_log; rank
+    0 recomputes each gathered round on its own GPU (the same kernels on the
+    same regenerated sequences) and requires bit equality, and dA_log within
+    1e-5 (its sum over sequences runs in another order).  Every N: the first
+    16 sequences against the CPU oracle at 2e-2 (bf16 I/O)."""
+    import numpy as np
     import torch
     import torch.distributed as dist
 
-    from hclsm_b200.kernels import ssm_scan_fn
-    from hclsm_b200.workloads import scan_inputs
+    from hclsm_b200.kernels.ssm_scan_kernel import scan_bwd_raw, scan_fwd_raw
+    from hclsm_b200.shard import shard_range
+    from hclsm_b200.workloads import scan_inputs_range
 
-    n = args.e2e_seqs
-    chunk = max(1, min(args.e2e_chunk, n))
-    host = {k: v.pin_memory() for k, v in scan_inputs(n, L, DI, DS, dtype=torch.bfloat16, seed=77 + rank).items()}
-    outs = {k: torch.empty_like(host["x"]).pin_memory() for k in ("y", "dx", "ddt")}
-    outs.update({k: torch.empty_like(host["B"]).pin_memory() for k in ("dB", "dC")})
-    dA_host = torch.empty(DI, DS, dtype=torch.float32).pin_memory()
+    out = {}
+    names = ("y", "dx", "ddt", "dB", "dC")
+    mine = dict(zip(names, (y, grads[0], grads[1], grads[3], grads[4])))
+    dA = grads[2].clone()
+    if world > 1:
+        blk = 64
+        ranges = [tuple(64 * v for v in shard_range(args.seqs // 64, r, world)) for r in range(world)]
+        rounds = max((e - s) // blk for s, e in ranges)
+        exact = True
+        for j in range(rounds):
+            gathered = {}
+            for k in names:
+                src = mine[k]
+                part = src[j * blk:(j + 1) * blk] if (j + 1) * blk <= src.shape[0] else torch.zeros_like(src[:blk])
+                buf = torch.empty((world * blk,) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
+                dist.all_gather_into_tensor(buf, part.contiguous())
+                gathered[k] = buf
+            if rank == 0:
+                for r, (s, e) in enumerate(ranges):
+                    if s + (j + 1) * blk > e:
+                        continue
+                    dd = scan_inputs_range(s + j * blk, blk, L, DI, DS, dtype=torch.bfloat16, seed=SEED, device=dev)
+                    yr = scan_fwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"])
+                    gr = scan_bwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], dd["dy"])
+                    ref = dict(zip(names, (yr, gr[0], gr[1], gr[3], gr[4])))
+                    for k in names:
+                        exact &= bool(torch.equal(gathered[k][r * blk:(r + 1) * blk], ref[k]))
+            del gathered
+        dist.all_reduce(dA)
+        # the single-GPU dA_log of the whole job, accumulated round by round on rank 0
+        if rank == 0:
+            tot = torch.zeros_like(dA)
+            for s in range(0, args.seqs, 1024):
+                dd = scan_inputs_range(s, min(1024, args.seqs - s), L, DI, DS, dtype=torch.bfloat16, seed=SEED,
+                                       device=dev)
+                tot += scan_bwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], dd["dy"])[2]
+            rel = float((dA - tot).abs().max() / tot.abs().max())
+            out.update({"gathered_bit_identical": exact, "dA_log_rel_err": rel})
+    if rank == 0 and shard[0] == 0:
+        from oracle import scan as oscan
+
+        n = 16
+        o = {k: d[k][:n].float().cpu().numpy() for k in ("x", "dt", "B", "C", "dy")}
+        A = d["A_log"].cpu().numpy()
+        yr = oscan.scan_fwd(o["x"], o["dt"], A, o["B"], o["C"])
+        gr = oscan.scan_bwd(o["x"], o["dt"], A, o["B"], o["C"], o["dy"])
+
+        def rel(a, b):
+            return float(np.abs(a - b).max() / np.abs(b).max())
+
+        errs = {"y": rel(y[:n].float().cpu().numpy(), yr)}
+        for k, gi in (("dx", 0), ("ddt", 1), ("dB", 3), ("dC", 4)):
+            errs[k] = rel(grads[gi][:n].float().cpu().numpy(), gr[k])
+        out["oracle_slice"] = {"sequences": n, "max_rel_err": max(errs.values()), "tol": 2e-2}
+    if rank == 0:
+        ok = out.get("gathered_bit_identical", True) and out.get("dA_log_rel_err", 0.0) < 1e-5 and \
+            out.get("oracle_slice", {"max_rel_err": 0.0})["max_rel_err"] < 2e-2
+        out["verified"] = bool(ok)
+    return out
+
+
+def run_e2e(args, rank, world, dev):
+    """The public API end to end: inputs in pinned host memory; per step the
+    H2D copy, ssm_scan_fn forward + autograd backward, and the D2H copy of y
+    and every gradient, for this rank's share of the config-4 job.  Chunks of
+    sequences are pipelined over an upload stream, the compute stream and a
+    download stream, so both PCIe directions run at once."""
+    import torch
+
+    from hclsm_b200.kernels import ssm_scan_fn
+    from hclsm_b200.shard import shard_range
+    from hclsm_b200.workloads import scan_inputs_range
+
+    s0, s1 = shard_range(args.seqs // 64, rank, world)
+    s0, s1 = s0 * 64, s1 * 64
+    n = s1 - s0
+    host = {}
+    for k, v in scan_inputs_range(s0, n, L, DI, DS, dtype=torch.bfloat16, seed=SEED, device=dev).items():
+        host[k] = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+        host[k].copy_(v)
+    torch.cuda.empty_cache()
+    outs = {k: torch.empty(host["x"].shape, dtype=host["x"].dtype, pin_memory=True) for k in ("y", "dx", "ddt")}
+    outs.update({k: torch.empty(host["B"].shape, dtype=host["B"].dtype, pin_memory=True) for k in ("dB", "dC")})
+    dA_host = torch.empty(DI, DS, dtype=torch.float32, pin_memory=True)
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = sum(v.numel() * v.element_size() for v in outs.values()) + dA_host.numel() * 4
     up = torch.cuda.Stream(dev)    # host -> device
     down = torch.cuda.Stream(dev)  # device -> host (the other PCIe direction)
     comp = torch.cuda.current_stream(dev)
-
+    chunk = 128
     # chunk boundaries: small chunks first and last, so that the pipeline's
     # fill (the first upload before any compute) and drain (the last download
     # after the last compute) are short
-    bounds, s0 = [], 0
-    ramp = [max(1, chunk // 4), max(1, chunk // 2)]
-    sizes = ramp + [chunk] * max(0, (n - 2 * sum(ramp)) // chunk)
-    rest = n - sum(sizes) - sum(ramp)
+    sizes = [32, 64] + [chunk] * max(0, (n - 192) // chunk)
+    rest = n - sum(sizes) - 96
     if rest > 0:
         sizes.append(rest)
-    sizes += ramp[::-1]
+    sizes += [64, 32]
+    bounds, a = [], 0
     for sz in sizes:
-        if s0 >= n:
+        if a >= n:
             break
-        bounds.append((s0, min(n, s0 + sz)))
-        s0 += sz
-    if s0 < n:
-        bounds.append((s0, n))
+        bounds.append((a, min(n, a + sz)))
+        a += sz
+    if a < n:
+        bounds.append((a, n))
 
     def step():
         # every host->device copy goes through the upload stream: the copy
@@ -230,182 +434,281 @@ def run_e2e(args, rank, world, dev):
         # all uploads already submitted and stall the compute stream
         with torch.cuda.stream(up):
             A = host["A_log"].to(dev, non_blocking=True)
-        for s0, s1 in bounds:
+        for c0, c1 in bounds:
             with torch.cuda.stream(up):
-                dv = {k: host[k][s0:s1].to(dev, non_blocking=True) for k in ("x", "dt", "B", "C", "dy")}
+                dv = {k: host[k][c0:c1].to(dev, non_blocking=True) for k in ("x", "dt", "B", "C", "dy")}
                 ready = torch.cuda.Event()
                 ready.record(up)
             comp.wait_event(ready)
-            if s0 == 0:
+            if c0 == 0:
                 A.record_stream(comp)
                 A.requires_grad_(True)
             for v in dv.values():
                 v.record_stream(comp)
             leaves = [dv[k].requires_grad_(True) for k in ("x", "dt", "B", "C")]
-            y = ssm_scan_fn(leaves[0], leaves[1], A, leaves[2], leaves[3])
-            torch.autograd.backward(y, dv["dy"])
+            yy = ssm_scan_fn(leaves[0], leaves[1], A, leaves[2], leaves[3])
+            torch.autograd.backward(yy, dv["dy"])
             done = torch.cuda.Event()
             done.record(comp)
             with torch.cuda.stream(down):
                 down.wait_event(done)
-                for k, t in (("y", y), ("dx", leaves[0].grad), ("ddt", leaves[1].grad),
+                for k, t in (("y", yy), ("dx", leaves[0].grad), ("ddt", leaves[1].grad),
                              ("dB", leaves[2].grad), ("dC", leaves[3].grad)):
-                    outs[k][s0:s1].copy_(t.detach(), non_blocking=True)
+                    outs[k][c0:c1].copy_(t.detach(), non_blocking=True)
                     t.record_stream(down)
         comp.wait_stream(down)
         dA_host.copy_(A.grad, non_blocking=True)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(comp)
     for _ in range(args.steps):
         step()
     e1.record(comp)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
-    return {"value": n * world / (ms * 1e-3), "unit": "sequences/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "sequences_per_rank": n}
+    (ms,) = _max_over_ranks([e0.elapsed_time(e1) / args.steps], dev, world)
+    del host, outs
+    return {"value": args.seqs / (ms * 1e-3), "unit": "sequences/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "sequences_per_rank": n,
+            "note": "per-rank bytes; copies from / to pinned host memory inside the timed region"}
 
 
-SLOT_FLOP_PER_FRAME = 7.29e10 / 128  # config 2: QK^T, attn V, W_q, GRU, MLP over 3 iterations + k/v proj
+# ---- legs for configs 0-3 ------------------------------------------------------------
+class L2Flush:
+    """Writes a buffer larger than L2 (126 MB) between timed iterations."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def __call__(self):
+        self.buf.zero_()
 
 
-def run_slot(args, rank, world, dev):
-    """Config 2: DynamicSlotAttention k/v projections + 3 fused iterations on 128
-    frames (32 slots, 196 tokens, dim 384, bf16), captured in a CUDA graph."""
+def _timed(fn, reps, dev, flush):
+    """Mean CUDA-event time (ms) of fn over reps calls, L2 flushed between calls
+    (outside the events)."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    tot = 0.0
+    for _ in range(reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        tot += e0.elapsed_time(e1)
+    return tot / reps
+
+
+def run_config0(args, rank, world, dev, peaks, flush):
+    """Config 0: ssm_scan_fn(backend="sequential") forward, fp32, with the D
+    skip and the SiLU gate: 32 sequences, L=16, d_inner=512, d_state=16."""
+    import torch
+
+    from hclsm_b200.kernels import ssm_scan_fn
+    from hclsm_b200.workloads import scan_inputs
+
+    d = scan_inputs(32, 16, 512, 16, dtype=torch.float32, seed=0, device=dev, gated=True, grad=False)
+
+    def call():
+        with torch.no_grad():
+            ssm_scan_fn(d["x"], d["dt"], d["A_log"], d["B"], d["C"], backend="sequential", D=d["D"], z=d["z"])
+
+    for _ in range(max(args.warmup, 10)):
+        call()
+    torch.cuda.synchronize(dev)
+    ms = _timed(call, 50, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    nbytes = 4 * 32 * 16 * 512 * 4 + 2 * 32 * 16 * 16 * 4 + 512 * 16 * 4 + 512 * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    leg = {"metric": "scan_fwd_latency_fp32", "value": ms, "unit": "ms", "higher_is_better": False,
+           "gbs_algorithmic": gbs, "algorithmic_bytes": nbytes,
+           "config": "BASELINE config 0: 32 sequences x L=16 x d_inner 512 x d_state 16, fp32, clamped "
+                     "(backend='sequential'), D skip + SiLU gate; L2 flushed between calls",
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks[0]["hbm_gbs"], "unit": "GB/s",
+                        "frac": gbs / peaks[0]["hbm_gbs"], "peak_source": peaks[1],
+                        "note": "4.3 MB per call: launch-latency bound (0.7 us at HBM speed)"}}
+    if rank == 0 and not args.no_cpu:
+        t = cpu_scan(32, 16, 512, 16, bwd=False, dtype_name="float32", gated=True)
+        leg["cpu_baseline"] = {"value": t * 1e3, "unit": "ms", "cores": _cpu_threads(), "kind": "port",
+                               "sample": "the whole config-0 call: sequential_ssm_scan restated in PyTorch on "
+                                         "the host (+ D skip and SiLU gate), best of 3"}
+    return leg
+
+
+def run_config1(args, rank, world, dev, peaks, flush):
+    """Config 1: ssm_scan_fn forward + autograd backward, bf16 in / fp32 state,
+    256 sequences x L=64 x d_inner 768 x d_state 16 (unclamped: the reference's
+    CUDA dispatch)."""
+    import torch
+
+    from hclsm_b200.kernels import ssm_scan_fn
+    from hclsm_b200.workloads import scan_inputs
+
+    d = scan_inputs(256, 64, 768, 16, dtype=torch.bfloat16, seed=1, device=dev)
+    leaves = {k: d[k].clone().requires_grad_(True) for k in ("x", "dt", "A_log", "B", "C")}
+
+    def step():
+        for t in leaves.values():
+            t.grad = None
+        y = ssm_scan_fn(leaves["x"], leaves["dt"], leaves["A_log"], leaves["B"], leaves["C"])
+        y.backward(d["dy"])
+
+    for _ in range(max(args.warmup, 5)):
+        step()
+    torch.cuda.synchronize(dev)
+    ms = _timed(step, 20, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    nbytes = 204_619_776
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    leg = {"metric": "scan_fwd_bwd_sequences_per_s", "value": 256 * world / (ms * 1e-3), "unit": "sequences/s",
+           "ms_per_step": ms, "gbs_algorithmic": gbs, "algorithmic_bytes": nbytes,
+           "config": "BASELINE config 1: 256 sequences x L=64 x d_inner 768 x d_state 16, bf16 I/O, fp32 state, "
+                     "fwd + bwd through ssm_scan_fn and autograd; L2 flushed between steps; per rank",
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks[0]["hbm_gbs"], "unit": "GB/s",
+                        "frac": gbs / peaks[0]["hbm_gbs"], "peak_source": peaks[1],
+                        "note": "whole step (fwd + bwd kernels + autograd glue); the kernels are SFU/issue bound"}}
+    if rank == 0 and not args.no_cpu:
+        n = 32
+        t = cpu_scan(n, 64, 768, 16, bwd=True, dtype_name="bfloat16", reps=2)
+        leg["cpu_baseline"] = {"value": n / t, "unit": "sequences/s", "cores": _cpu_threads(), "kind": "port",
+                               "sample": f"{n} of the 256 config-1 sequences, fwd + autograd bwd of "
+                                         "sequential_ssm_scan restated in PyTorch on the host, best of 2"}
+    return leg
+
+
+def run_slot(args, rank, world, dev, peaks, flush):
+    """Config 2: DynamicSlotAttention k/v projections + 3 fused iterations on
+    128 frames (32 slots, 196 tokens, dim 384, bf16), frames sharded over the
+    ranks, as one CUDA graph.  Verification: NCCL all-gather of every rank's
+    slots to rank 0 against rank 0's run of all 128 frames."""
     import torch
     import torch.distributed as dist
 
     from hclsm_b200.kernels import SlotIterationParams, slot_attention_iterations
+    from hclsm_b200.shard import shard_range
     from hclsm_b200.workloads import slot_inputs
 
-    d = slot_inputs(seed=10 + rank, device=dev)
+    d = slot_inputs(seed=10, device=dev)
     W = d["weights"]
     p = SlotIterationParams.from_state(W, dev)
     wk = W["project_k.weight"].to(torch.bfloat16).t().contiguous()
     wv = W["project_v.weight"].to(torch.bfloat16).t().contiguous()
-    inp = d["inputs"].to(torch.bfloat16)
-    F_, M, D = inp.shape
+    f0, f1 = shard_range(128, rank, world)
+    inp_all = d["inputs"].to(torch.bfloat16)
+    slots_all = d["slots"]
 
-    def step():
+    def run(inp, slots):
+        F_, M, D = inp.shape
         x = inp.reshape(F_ * M, D)
         k = torch.mm(x, wk).reshape(F_, M, D)
         v = torch.mm(x, wv).reshape(F_, M, D)
-        return slot_attention_iterations(d["slots"], k, v, p, 3)
+        return slot_attention_iterations(slots, k, v, p, 3)
 
+    inp, slots = inp_all[f0:f1].contiguous(), slots_all[f0:f1].contiguous()
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
         for _ in range(args.warmup):
-            step()
+            run(inp, slots)
     torch.cuda.current_stream(dev).wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        step()
+        out = run(inp, slots)
     for _ in range(args.warmup):
         g.replay()
-    reps = 20
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
+    _barrier(world)
+    ms = _timed(g.replay, 20, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    frames = f1 - f0
+    tflops = SLOT_FLOP_PER_FRAME * 128 / (ms * 1e-3) / 1e12
+    peak = peaks[0].get("bf16_tflops_sustained", peaks[0]["bf16_tflops"])
+    leg = {"metric": "slot_attention_frames_per_s", "value": 128 / (ms * 1e-3), "unit": "frames/s",
+           "ms_per_step": ms, "frames_per_rank": frames, "scaling": "strong",
+           "config": "BASELINE config 2: 128 frames x 32 slots x 196 tokens x 384, 3 iterations, bf16, k/v "
+                     "projections included, frames sharded over ranks, CUDA graph; L2 flushed between replays",
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tflops / peak, "peak_source": peaks[1] + " bf16_tflops_sustained",
+                        "flop_per_step": SLOT_FLOP_PER_FRAME * 128}}
+    if world > 1 and not args.no_verify:
         g.replay()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
-    return {"metric": "slot_attention_frames_per_s", "value": F_ * world / (ms * 1e-3), "unit": "frames/s",
-            "ms_per_step": ms, "config": "BASELINE config 2: 128 frames x 32 slots x 196 tokens x 384, 3 iterations, "
-                                         "bf16, k/v projections included, CUDA graph",
-            "tflops": SLOT_FLOP_PER_FRAME * F_ / (ms * 1e-3) / 1e12}
+        full = [torch.empty((shard_range(128, r, world)[1] - shard_range(128, r, world)[0],) + tuple(out.shape[1:]),
+                            dtype=out.dtype, device=dev) for r in range(world)]
+        dist.all_gather(full, out)
+        if rank == 0:
+            ref = run(inp_all, slots_all)
+            got = torch.cat(full, 0)
+            leg["verify"] = {"rel_err_vs_single_gpu": float((got - ref).abs().max() / ref.abs().max()),
+                             "tol": 2e-2}
+            leg["verify"]["verified"] = leg["verify"]["rel_err_vs_single_gpu"] < 2e-2
+    if rank == 0 and not args.no_cpu:
+        t = cpu_slot()
+        leg["cpu_baseline"] = {"value": 128 / t, "unit": "frames/s", "cores": _cpu_threads(), "kind": "port",
+                               "sample": "the whole config-2 step (k/v projections + 3 x _iteration_step restated "
+                                         "in PyTorch, fp32) on the host, best of 3"}
+    del g
+    return leg
 
 
-def run_event(args, rank, world, dev):
-    """Config 3: sparse event attention with the 3-layer Level-1 transformer over
-    8 videos x 64 steps x 32 slots x 384 (bf16), Bernoulli(0.1) event mask."""
+def run_event(args, rank, world, dev, peaks, flush):
+    """Config 3: sparse event attention with the 3-layer Level-1 transformer
+    over 8 videos x 64 steps x 32 slots x 384 (bf16), Bernoulli(0.1) mask;
+    videos sharded over the ranks.  Verification as the slot leg."""
     import torch
     import torch.distributed as dist
 
     from hclsm_b200.kernels import EventTransformer, sparse_event_attn_fn
+    from hclsm_b200.shard import shard_range
     from hclsm_b200.workloads import event_inputs
 
-    d = event_inputs(seed=20 + rank, device=dev)
-    tr = EventTransformer.from_state(d["weights"], d["heads"], dev, dtype=torch.bfloat16)
-    st = d["states"].to(torch.bfloat16)
-    m = d["mask"]
+    e = event_inputs(seed=20, device=dev)
+    tr = EventTransformer.from_state(e["weights"], e["heads"], dev, dtype=torch.bfloat16)
+    st_all = e["states"].to(torch.bfloat16)
+    m_all = e["mask"]
+    v0, v1 = shard_range(8, rank, world)
+    st, m = st_all[v0:v1].contiguous(), m_all[v0:v1].contiguous()
     for _ in range(args.warmup):
         sparse_event_attn_fn(st, m, tr)
-    reps = 20
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        sparse_event_attn_fn(st, m, tr)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
-    n_ev = int(m.sum().item())
-    return {"metric": "sparse_event_attention_events_per_s", "value": n_ev * world / (ms * 1e-3),
-            "unit": "event frames/s", "ms_per_call": ms, "event_frames": n_ev,
-            "config": "BASELINE config 3: 8 videos x 64 steps x 32 slots x 384, 6 heads, 3 layers, p=0.1, bf16"}
-
-
-def run_ssm_block(args, rank, world, dev):
-    """SimplifiedSSMBlock forward + backward (hclsm_b200.install's patched
-    forward: LayerNorm, projections, softplus(dt) + clamp + scan + SiLU gate in
-    one kernel, out_proj, residual) under bf16 autocast, on config-1 scan
-    shapes: 256 sequences x T=64, d_model 384 (d_inner 768), d_state 16."""
-    import torch
-    import torch.distributed as dist
-
-    from hclsm_b200.install import _ssm_block_forward
-    from hclsm_b200.workloads import ssm_block_inputs
-
-    blk, x = ssm_block_inputs(seed=30 + rank, device=dev)
-    x.requires_grad_(True)
-
-    def step():
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            y = _ssm_block_forward(blk, x)
-        y.float().sum().backward()
-
-    for _ in range(args.warmup):
-        step()
-    reps = 20
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        step()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
-    return {"metric": "ssm_block_fwd_bwd_sequences_per_s", "value": x.shape[0] * world / (ms * 1e-3),
-            "unit": "sequences/s", "ms_per_step": ms,
-            "config": "SimplifiedSSMBlock fwd+bwd, 256 sequences x T=64 x d_model 384 (d_inner 768, d_state 16), "
-                      "bf16 autocast, softplus(dt) fused into the scan"}
+    _barrier(world)
+    ms = _timed(lambda: sparse_event_attn_fn(st, m, tr), 20, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    n_ev = int(m_all.sum().item())
+    tflops = EVENT_FLOP_PER_FRAME * n_ev / (ms * 1e-3) / 1e12
+    peak = peaks[0].get("bf16_tflops_sustained", peaks[0]["bf16_tflops"])
+    leg = {"metric": "sparse_event_attention_events_per_s", "value": n_ev / (ms * 1e-3),
+           "unit": "event frames/s", "ms_per_call": ms, "event_frames": n_ev, "videos_per_rank": v1 - v0,
+           "scaling": "strong",
+           "config": "BASELINE config 3: 8 videos x 64 steps x 32 slots x 384, 6 heads, 3 layers, p=0.1, bf16, "
+                     "videos sharded over ranks; L2 flushed between calls",
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tflops / peak, "peak_source": peaks[1] + " bf16_tflops_sustained",
+                        "flop_per_event_frame": EVENT_FLOP_PER_FRAME,
+                        "note": "about 4e9 FLOP per call: launch / latency bound"}}
+    if world > 1 and not args.no_verify:
+        out = sparse_event_attn_fn(st, m, tr)
+        full = [torch.empty((shard_range(8, r, world)[1] - shard_range(8, r, world)[0],) + tuple(out.shape[1:]),
+                            dtype=out.dtype, device=dev) for r in range(world)]
+        dist.all_gather(full, out)
+        if rank == 0:
+            ref = sparse_event_attn_fn(st_all, m_all, tr)
+            got = torch.cat(full, 0).float()
+            r = float((got - ref.float()).abs().max() / ref.float().abs().max())
+            leg["verify"] = {"rel_err_vs_single_gpu": r, "tol": 2e-2, "verified": r < 2e-2}
+    if rank == 0 and not args.no_cpu:
+        t, nev = cpu_event()
+        leg["cpu_baseline"] = {"value": nev / t, "unit": "event frames/s", "cores": _cpu_threads(), "kind": "port",
+                               "sample": "the whole config-3 call (naive_sparse_event_attention + the Level-1 "
+                                         "stack restated in PyTorch, fp32) on the host, best of 3"}
+    return leg
 
 
 def main():
@@ -414,24 +717,31 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     args.warmup = max(args.warmup, 3)
+    if args.seqs % (64 * world):
+        raise SystemExit("--seqs must be a multiple of 64 x world size")
     metric = "ssm_scan_fwd_bwd_throughput"
     config = {"workload": "BASELINE config 4: selective scan fwd+bwd, 64 videos x 128 slots = 8192 sequences "
-                          "per GPU, L=256, d_inner=2048, d_state=16, bf16 I/O / fp32 state",
-              "sequences_per_gpu": args.seqs, "global_sequences": args.seqs * world, "L": L,
+                          "in one job, L=256, d_inner=2048, d_state=16, bf16 I/O / fp32 state, sequences sharded "
+                          "over the GPUs",
+              "global_sequences": args.seqs, "sequences_per_gpu": args.seqs // world, "L": L,
               "d_inner": DI, "d_state": DS, "parallelism": f"sequence-sharded x{world}",
-              "l2": "inputs (8.6 GB per tensor) are larger than L2; no flush needed"}
+              "l2": "inputs (8.6 GB per tensor at N=1, 1.07 GB at N=8) are larger than L2; no flush needed"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        val, cores, step_s = cpu_reference(args.ref_seqs, args.steps, 1)
+        n = args.ref_seqs
+        sec = cpu_scan(n, L, DI, DS, bwd=True, dtype_name="bfloat16", reps=args.steps, seed=1234)
+        val = n / sec
         line = {"metric": metric, "value": val, "unit": "sequences/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "impl": "reference",
-                "cpu_baseline": {"value": val, "unit": "sequences/s", "cores": cores, "kind": "port",
-                                 "sample": f"{args.ref_seqs} config-4 sequences fwd+bwd per step (C restatement "
-                                           f"of the reference scan on bf16-rounded inputs, fp32 arithmetic)"},
+                "cpu_baseline": {"value": val, "unit": "sequences/s", "cores": _cpu_threads(), "kind": "port",
+                                 "sample": f"{n} config-4 sequences per step: sequential_ssm_scan + autograd "
+                                           "backward (hclsm/kernels/ssm_scan_kernel.py:42-86, the reference's CPU "
+                                           "path) restated op for op in PyTorch, fp32 on bf16-rounded inputs, "
+                                           "best step"},
                 "e2e": {"value": val, "unit": "sequences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -439,48 +749,55 @@ def main():
     import torch
     import torch.distributed as dist
 
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    r = run_b200(args, rank, world, local_rank)
     dev = torch.device("cuda", local_rank)
-    slot = None if args.no_extra else run_slot(args, rank, world, dev)
-    event = None if args.no_extra else run_event(args, rank, world, dev)
-    block = None if args.no_extra else run_ssm_block(args, rank, world, dev)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    peaks = _peaks()
+    r = run_config4(args, rank, world, dev)
+    e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)
+    legs = {}
+    if not args.no_extra:
+        flush = L2Flush(dev)
+        legs["config0"] = run_config0(args, rank, world, dev, peaks, flush)
+        legs["config1"] = run_config1(args, rank, world, dev, peaks, flush)
+        legs["config2_slot_attention"] = run_slot(args, rank, world, dev, peaks, flush)
+        legs["config3_event_attention"] = run_event(args, rank, world, dev, peaks, flush)
+        del flush
     cpu = None
     if rank == 0 and not args.no_cpu:
-        v, cores, _ = cpu_reference(args.ref_seqs, 1, 1)
-        cpu = {"value": v, "unit": "sequences/s", "cores": cores, "kind": "port",
-               "sample": f"{args.ref_seqs} config-4 sequences fwd+bwd (C restatement of the reference scan)"}
-    if world > 1:
-        dist.barrier()
+        n = args.ref_seqs
+        sec = cpu_scan(n, L, DI, DS, bwd=True, dtype_name="bfloat16", reps=1, seed=1234)
+        sec_c, thr_c = cpu_scan_c(16)
+        cpu = {"value": n / sec, "unit": "sequences/s", "cores": _cpu_threads(), "kind": "port",
+               "sample": f"{n} config-4 sequences fwd + autograd bwd of sequential_ssm_scan restated op for op in "
+                         f"PyTorch on the host (the reference's CPU path)",
+               "c_restatement": {"value": 16 / sec_c, "unit": "sequences/s", "cores": thr_c,
+                                 "sample": "16 config-4 sequences fwd + bwd, the C restatement of the scan"}}
+    _barrier(world)
     if rank == 0:
         ms = r["ms_per_step"]
-        fwd_bytes = args.seqs * FWD_BYTES_PER_SEQ + ALOG_BYTES
-        bwd_bytes = args.seqs * BWD_BYTES_PER_SEQ + 2 * ALOG_BYTES
-        peaks = {}
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peaks = json.load(f)
-        except OSError:
-            pass
-        hbm_peak = peaks.get("hbm_gbs", 6650.0)
+        nloc = r["seqs_per_rank"]
+        fwd_bytes = nloc * FWD_BYTES_PER_SEQ + ALOG_BYTES
+        bwd_bytes = nloc * BWD_BYTES_PER_SEQ + 2 * ALOG_BYTES
+        hbm = peaks[0]["hbm_gbs"]
         bw_bwd = bwd_bytes / (r["bwd_ms"] * 1e-3) / 1e9
         bw_fwd = fwd_bytes / (r["fwd_ms"] * 1e-3) / 1e9
-        line = {"metric": metric, "value": args.seqs * world / (ms * 1e-3), "unit": "sequences/s",
+        line = {"metric": metric, "value": args.seqs / (ms * 1e-3), "unit": "sequences/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": config,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded, BASELINE distributions)", "config": config,
                 "hbm_gbs_algorithmic": (fwd_bytes + bwd_bytes) * world / (ms * 1e-3) / 1e9,
                 "roofline": {"bound": "hbm", "kernel": "scan_bwd_bf16_kernel (hclsm_ssm_scan_bwd_states)",
-                             "achieved": bw_bwd, "peak": hbm_peak, "unit": "GB/s", "frac": bw_bwd / hbm_peak,
-                             "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                             "traffic": BWD_TRAFFIC_PER_SEQ * args.seqs, "algorithmic_bytes": bwd_bytes,
-                             "ms": r["bwd_ms"]},
+                             "achieved": bw_bwd, "peak": hbm, "unit": "GB/s", "frac": bw_bwd / hbm,
+                             "peak_source": peaks[1], "traffic": BWD_TRAFFIC_PER_SEQ * nloc,
+                             "algorithmic_bytes": bwd_bytes, "ms": r["bwd_ms"],
+                             "exp_floor_ms": nloc * L * DI * DS / (16 * 148 * 1.965e9) * 1e3},
                 "roofline_fwd": {"kernel": "scan_fwd_bf16x2_kernel (hclsm_ssm_scan_fwd_states)", "achieved": bw_fwd,
-                                 "frac": bw_fwd / hbm_peak, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes},
-                "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
-                "slot_attention": slot, "event_attention": event, "ssm_block": block,
-                "gpu_launches": 5 * args.steps}
+                                 "frac": bw_fwd / hbm, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes,
+                                 "exp_floor_ms": nloc * L * DI * DS / (16 * 148 * 1.965e9) * 1e3},
+                "verify": r.get("verify"), "cpu_baseline": cpu, "e2e": e2e, "clocks": r["clocks"],
+                "legs": legs, "gpu_launches": 5 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -56,6 +56,16 @@ SIGNATURES = {
     "hclsm_event_scatter": (ctypes.c_int, [_vp] * 5 + [_i64, _i64, _i32, _i32, _i32, _vp]),
     "hclsm_event_mha": (ctypes.c_int, [_vp] * 3 + [_i32] * 4 + [ctypes.c_float, _i32, _vp]),
     "hclsm_swiglu": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _vp]),
+    "hclsm_colsum_workspace_size": (_sz, [_i32]),
+    "hclsm_colsum": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _sz, _vp]),
+    "hclsm_layernorm_bwd_workspace_size": (_sz, [_i64, _i32]),
+    "hclsm_layernorm_bwd": (ctypes.c_int, [_vp] * 6 + [_i64, _i32, ctypes.c_float, _i32, _vp, _sz, _vp]),
+    "hclsm_gru_cell_bwd": (ctypes.c_int, [_vp] * 9 + [_i64, _i32, _vp]),
+    "hclsm_slot_softmax_bwd": (ctypes.c_int, [_vp] * 4 + [_i32] * 3 + [ctypes.c_float] * 3 + [_i32, _vp]),
+    "hclsm_residual_clamp_bwd": (ctypes.c_int, [_vp] * 5 + [_i64, _i32, ctypes.c_float, _vp]),
+    "hclsm_relu_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _i64, _vp]),
+    "hclsm_swiglu_bwd": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "hclsm_event_mha_bwd": (ctypes.c_int, [_vp] * 4 + [_i32] * 4 + [ctypes.c_float, _i32, _vp]),
     "hclsm_ssm_scan_bwd_noalloc_max_scratch": (_sz, []),
     "hclsm_ssm_scan_bwd_noalloc": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
 }

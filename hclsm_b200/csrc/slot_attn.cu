@@ -512,10 +512,8 @@ extern "C" int hclsm_slot_attn_core(const void* Q, const void* K, const void* V,
   if (!al(Q) || !al(K) || !al(V) || !al(out)) return HCLSM_ERR_ALIGN;
   // tcgen05 core for the shapes it covers; HCLSM_SLOT_CORE=mma selects the
   // mma.sync core (used by the tests to check one against the other)
-  static const bool force_mma = [] {
-    const char* e = std::getenv("HCLSM_SLOT_CORE");
-    return e && std::strcmp(e, "mma") == 0;
-  }();
+  const char* sel = std::getenv("HCLSM_SLOT_CORE");  // read per call, as the tests switch it
+  const bool force_mma = sel && std::strcmp(sel, "mma") == 0;
   if (!force_mma) {
     const int rc = slot_core_tc(Q, K, V, out, attn, F, N, M, D, scale, clamp, eps, attn_f32, st);
     if (rc != HCLSM_ERR_UNSUPPORTED) return rc;

@@ -25,11 +25,14 @@ What is replaced (paths inside RightNow-AI/hclsm):
   (hclsm/dynamics/hierarchy_manager.py:42-118);
 * ``Level1EventDynamics.forward`` (hclsm/dynamics/level1_event.py:85-133).
 
-The scan is differentiable.  The slot-attention step, the event gather /
-scatter and the Level-1 transformer are forward kernels: they replace the
-reference while autograd is off (inference, planning, evaluation) and defer to
-the reference's own implementation while a gradient is being recorded.  CPU
-tensors are not accepted by the replaced functions (no CPU fallback).
+Every replaced call site is differentiable through this library's kernels:
+the scan and the Level-0 epilogue have backward kernels, and the slot-attention
+step, the event gather / scatter and the Level-1 transformer run as autograd
+Functions (hclsm_b200.kernels.training) whenever a gradient is recorded, with
+cheaper forward-only kernels otherwise.  The weight products follow the
+caller's arithmetic: bf16 operands under bf16 autocast or for bf16 inputs,
+fp32 otherwise.  CPU tensors are not accepted by the replaced functions (no CPU
+fallback).
 """
 from __future__ import annotations
 
@@ -40,6 +43,22 @@ _ORIG = {}
 
 def _grad_active(*tensors):
     return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def _module_grad(mod, *tensors):
+    """True when autograd records through ``mod``'s call (an input or a
+    parameter requires grad)."""
+    if not torch.is_grad_enabled():
+        return False
+    return _grad_active(*tensors) or any(p.requires_grad for p in mod.parameters())
+
+
+def _work_dtype(*tensors):
+    """Arithmetic of the weight products: bf16 under bf16 autocast or for bf16
+    inputs (the reference's autocast arithmetic), else fp32."""
+    if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        return torch.bfloat16
+    return torch.bfloat16 if any(t is not None and t.dtype == torch.bfloat16 for t in tensors) else torch.float32
 
 
 def _patch(obj, name, new):
@@ -80,18 +99,21 @@ def _ssm_block_forward(self, x):
 
 def _make_iteration_step(orig):
     def _iteration_step(self, slots, k, v):
-        if _grad_active(slots, k, v) or any(p.requires_grad for p in self.parameters()) and torch.is_grad_enabled():
-            return orig(self, slots, k, v)
         from .kernels.slot_attention_kernel import SlotIterationParams, slot_attention_iteration
 
-        key = tuple(p._version for p in self.parameters())
+        dt = _work_dtype(slots, k, v)
+        if _module_grad(self, slots, k, v):
+            from .kernels.training import slot_iteration_train
+
+            return slot_iteration_train(self, slots, k, v, dt).to(slots.dtype)
+        key = (tuple(p._version for p in self.parameters()), dt)
         cache = getattr(self, "_hclsm_b200_params", None)
         if cache is None or cache[0] != key:
-            cache = (key, SlotIterationParams.from_module(self))
+            cache = (key, SlotIterationParams.from_module(self, dt))
             self._hclsm_b200_params = cache
-        kb = k.to(torch.bfloat16).contiguous()
-        vb = v.to(torch.bfloat16).contiguous()
-        out, _ = slot_attention_iteration(slots.float().contiguous(), kb, vb, cache[1])
+        kd = k.to(dt).contiguous()
+        vd = v.to(dt).contiguous()
+        out, _ = slot_attention_iteration(slots.float().contiguous(), kd, vd, cache[1])
         return out.to(slots.dtype)
 
     return _iteration_step
@@ -142,18 +164,21 @@ def _make_dsa_forward(orig):
 
 def _make_gather(orig):
     def gather_events(self, states, event_mask):
-        if _grad_active(states):
-            return orig(self, states, event_mask)
-        from .kernels.sparse_event_attn import event_compact, event_gather
+        from .kernels.sparse_event_attn import _cached_compaction, event_compact, event_gather
 
         B, T, N, D = states.shape
         st = states.contiguous()
-        cached = getattr(event_mask, "_hclsm_events", None)  # from the patched EventDetector
+        cached = _cached_compaction(event_mask)  # from the patched EventDetector
         idx, pos, counts, meta = cached if cached is not None else event_compact(event_mask)
         kmax = max(int(meta[1].item()), 1)
         if cached is not None:
             event_mask._hclsm_kmax = kmax
-        ev = event_gather(st, idx, counts, meta, B * kmax, pad_k=kmax).reshape(B, kmax, N, D)
+        if _grad_active(states):
+            from .kernels.training import event_gather_train
+
+            ev = event_gather_train(states, idx, pos, counts, meta, kmax)
+        else:
+            ev = event_gather(st, idx, counts, meta, B * kmax, pad_k=kmax).reshape(B, kmax, N, D)
         pad = (torch.arange(kmax, device=states.device)[None, :] < counts[:B, None]).float()
         return ev, pad, kmax
 
@@ -162,18 +187,20 @@ def _make_gather(orig):
 
 def _make_scatter(orig):
     def scatter_events(self, base_states, event_updates, event_mask):
-        if _grad_active(base_states, event_updates):
-            return orig(self, base_states, event_updates, event_mask)
-        from .kernels.sparse_event_attn import event_compact, event_scatter
+        from .kernels.sparse_event_attn import _cached_compaction, event_compact, event_scatter
 
         K = event_updates.shape[1]
-        cached = getattr(event_mask, "_hclsm_events", None)
+        cached = _cached_compaction(event_mask)
         if cached is not None and K >= getattr(event_mask, "_hclsm_kmax", K + 1):
             idx, pos, counts, meta = cached  # every event fits: the detector's compaction as is
         else:
             m = (event_mask > 0.5)
             rank = torch.cumsum(m.int(), dim=1) - 1
             idx, pos, counts, meta = event_compact((m & (rank < K)).float())
+        if _grad_active(base_states, event_updates):
+            from .kernels.training import event_scatter_train
+
+            return event_scatter_train(base_states, event_updates, idx, pos, counts, meta, K)
         upd = event_updates.reshape(-1, *event_updates.shape[2:]).to(base_states.dtype).contiguous()
         return event_scatter(base_states.contiguous(), upd, pos, counts, pad_k=K)
 
@@ -206,21 +233,24 @@ def _make_detector_forward(orig):
 
 def _make_level1_forward(orig):
     def forward(self, event_states, event_pad_mask=None, obj_mask=None):
-        if _grad_active(event_states) or any(p.requires_grad for p in self.parameters()) and torch.is_grad_enabled():
-            return orig(self, event_states, event_pad_mask, obj_mask)
         from .kernels.sparse_event_attn import EventTransformer
 
-        key = tuple(p._version for p in self.parameters())
-        cache = getattr(self, "_hclsm_b200_tr", None)
-        dtype = torch.bfloat16 if event_states.dtype == torch.bfloat16 else torch.float32
-        if cache is None or cache[0] != (key, dtype):
-            cache = ((key, dtype), EventTransformer.from_module(self, dtype))
-            self._hclsm_b200_tr = cache
+        dtype = _work_dtype(event_states)
         B, K, N, D = event_states.shape
         kp = None
         if obj_mask is not None:
             kp = (~(obj_mask > 0.5)).unsqueeze(1).expand(B, K, N).reshape(B * K, N)
-        y = cache[1](event_states.reshape(B * K, N, D), kp).reshape(B, K, N, -1)
+        if _module_grad(self, event_states):
+            from .kernels.training import level1_train
+
+            y = level1_train(self, event_states.reshape(B * K, N, D), kp, dtype).reshape(B, K, N, -1)
+        else:
+            key = tuple(p._version for p in self.parameters())
+            cache = getattr(self, "_hclsm_b200_tr", None)
+            if cache is None or cache[0] != (key, dtype):
+                cache = ((key, dtype), EventTransformer.from_module(self, dtype))
+                self._hclsm_b200_tr = cache
+            y = cache[1](event_states.reshape(B * K, N, D), kp).reshape(B, K, N, -1)
         if event_pad_mask is not None:
             y = y * event_pad_mask[:, :, None, None]
         return y

@@ -137,8 +137,11 @@ def residual_clamp(h, m, b, clamp=50.0, out=None, out_bf16=None):
 @dataclass
 class SlotIterationParams:
     """Parameters of DynamicSlotAttention used by _iteration_step (names as in
-    hclsm/objects/dynamic_slots.py:44-83), prepared once: weights in bf16
-    (transposed for x @ W^T), biases and LayerNorm affines in fp32."""
+    hclsm/objects/dynamic_slots.py:44-83), prepared once: weights in ``dtype``
+    (transposed for x @ W^T), biases and LayerNorm affines in fp32.  ``dtype``
+    is the arithmetic of the weight products: bfloat16 (the reference under
+    bf16 autocast; fp32 accumulation and outputs) or float32 (the reference
+    without autocast: every product in fp32)."""
     wq_t: torch.Tensor
     w_ih_t: torch.Tensor
     w_hh_t: torch.Tensor
@@ -153,12 +156,16 @@ class SlotIterationParams:
     ln_mlp_w: torch.Tensor
     ln_mlp_b: torch.Tensor
     scale: float
-    b1_bf16: torch.Tensor | None = None  # the MLP's first bias for the fused GEMM epilogue
+    b1_bf16: torch.Tensor | None = None  # the MLP's first bias for the fused GEMM epilogue (bf16 path)
+    dtype: torch.dtype = torch.bfloat16
 
     @classmethod
-    def from_state(cls, sd: dict, device, d_slot: int | None = None):
+    def from_state(cls, sd: dict, device, d_slot: int | None = None, dtype=torch.bfloat16):
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"hclsm_b200: slot iteration dtype {dtype} (bfloat16 or float32)")
+
         def w(name):
-            return sd[name].detach().to(device=device, dtype=torch.bfloat16).t().contiguous()
+            return sd[name].detach().to(device=device, dtype=dtype).t().contiguous()
 
         def f(name):
             return sd[name].detach().to(device=device, dtype=torch.float32).contiguous()
@@ -168,49 +175,57 @@ class SlotIterationParams:
         return cls(w("project_q.weight"), w("gru.weight_ih"), w("gru.weight_hh"), f("gru.bias_ih"),
                    f("gru.bias_hh"), w("mlp.0.weight"), b1, w("mlp.2.weight"), f("mlp.2.bias"),
                    f("norm_pre_attn.weight"), f("norm_pre_attn.bias"), f("norm_slots.weight"),
-                   f("norm_slots.bias"), D ** -0.5, b1.to(torch.bfloat16))
+                   f("norm_slots.bias"), D ** -0.5, b1.to(torch.bfloat16) if dtype == torch.bfloat16 else None,
+                   dtype)
 
     @classmethod
-    def from_module(cls, mod):
-        return cls.from_state(dict(mod.named_parameters()), next(mod.parameters()).device, mod.d_slot)
+    def from_module(cls, mod, dtype=torch.bfloat16):
+        return cls.from_state(dict(mod.named_parameters()), next(mod.parameters()).device, mod.d_slot, dtype)
 
 
 def _mm(a, w_t):
+    if a.dtype == torch.float32:
+        return torch.mm(a, w_t)
     return torch.mm(a, w_t, out_dtype=torch.float32)
 
 
-def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_bf16=None):
+def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_lp=None):
     """One _iteration_step (dynamic_slots.py:98-131).  slots (F, N, D) fp32 (the
-    carried state), k and v (F, M, D) bf16.  Returns (slots_new fp32, bf16 copy)."""
+    carried state), k and v (F, M, D) in ``p.dtype``.  Returns (slots_new fp32,
+    a bf16 copy of it on the bf16 path, else None)."""
     F, N, D = slots.shape
     R = F * N
+    dt = p.dtype
     s2 = slots.reshape(R, D)
-    if slots_bf16 is None:
-        slots_bf16 = s2.to(torch.bfloat16)
-    sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=torch.bfloat16)
+    lp = dt == torch.bfloat16
+    if lp and slots_lp is None:
+        slots_lp = s2.to(torch.bfloat16)
+    sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=dt)
     q = torch.mm(sn, p.wq_t).reshape(F, N, D)
     upd, _ = slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False)
     gi = _mm(upd.reshape(R, D), p.w_ih_t)
-    gh = _mm(slots_bf16.reshape(R, D), p.w_hh_t)
+    gh = _mm(slots_lp.reshape(R, D) if lp else s2, p.w_hh_t)
     h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
-    m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=torch.bfloat16)
-    if p.b1_bf16 is not None:
+    m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=dt)
+    if lp and p.b1_bf16 is not None:
         # bias + ReLU in the library GEMM's epilogue, bf16 out (the MLP runs in
         # the autocast dtype in the reference)
         m = torch._addmm_activation(p.b1_bf16, m, p.w1_t)
+    elif not lp:
+        m = torch._addmm_activation(p.b1, m, p.w1_t)  # fp32 throughout
     else:
         m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
     m = _mm(m, p.w2_t)
-    out_bf = torch.empty(R, D, dtype=torch.bfloat16, device=slots.device)
-    out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_bf)
-    return out.reshape(F, N, D), out_bf.reshape(F, N, D)
+    out_lp = torch.empty(R, D, dtype=torch.bfloat16, device=slots.device) if lp else None
+    out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_lp)
+    return out.reshape(F, N, D), (out_lp.reshape(F, N, D) if lp else None)
 
 
 def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations: int):
     s = slots.float().contiguous()
-    sb = None
-    k = _c(k.to(torch.bfloat16))
-    v = _c(v.to(torch.bfloat16))
+    sl = None
+    k = _c(k.to(p.dtype))
+    v = _c(v.to(p.dtype))
     for _ in range(n_iterations):
-        s, sb = slot_attention_iteration(s, k, v, p, sb)
+        s, sl = slot_attention_iteration(s, k, v, p, sl)
     return s

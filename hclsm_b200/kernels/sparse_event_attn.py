@@ -82,13 +82,19 @@ def event_detect(event_probs, threshold):
     first = torch.zeros(B, T, dtype=torch.bool, device=dev)
     first[:, 0] = True
     mask = torch.where(first & (meta[2] > 0), torch.ones((), dtype=mask.dtype, device=dev), mask)
-    mask._hclsm_events = (idx, pos, counts, meta)
+    # tagged with the mask's version: an in-place edit of the mask afterwards
+    # invalidates the compaction (the gather / scatter then recompact)
+    mask._hclsm_events = (mask._version, (idx, pos, counts, meta))
     return mask
 
 
 def _cached_compaction(event_mask):
-    """The compaction event_detect attached to this mask, or None."""
-    return getattr(event_mask, "_hclsm_events", None)
+    """The compaction event_detect attached to this mask, or None when there is
+    none or the mask was modified in place since."""
+    ent = getattr(event_mask, "_hclsm_events", None)
+    if ent is None or ent[0] != event_mask._version:
+        return None
+    return ent[1]
 
 
 def event_gather(states, idx, counts, meta, n_frames, pad_k=0, out=None):

@@ -62,6 +62,35 @@ def scan_inputs(nseq, L, d_inner, d_state, dtype=torch.float32, seed=0, device="
     return out
 
 
+def scan_inputs_range(start, nseq, L, d_inner, d_state, dtype=torch.bfloat16, seed=0, device="cpu", block=64):
+    """Sequences [start, start + nseq) of a global seeded config-4 style job:
+    x, dt, B, C, dy with the distributions of ``scan_inputs``, drawn per block
+    of ``block`` sequences from a generator seeded by (seed, block index), so
+    any shard of the job (start and nseq multiples of ``block``) regenerates
+    exactly the sequences a single-GPU run of the whole job sees.  A_log
+    depends on the seed only."""
+    if start % block or nseq % block:
+        raise ValueError("start and nseq must be multiples of the block size")
+    g = torch.Generator(device=device).manual_seed(seed)
+    A_log = torch.rand(d_inner, d_state, generator=g, device=device) * math.log(16.0)
+    out = {k: torch.empty(nseq, L, d_inner if k in ("x", "dt", "dy") else d_state, dtype=dtype, device=device)
+           for k in ("x", "dt", "B", "C", "dy")}
+    for i in range(nseq // block):
+        gb = torch.Generator(device=device).manual_seed(seed * 1000003 + start // block + i)
+        sl = slice(i * block, (i + 1) * block)
+
+        def randn(*shape):
+            return torch.randn(block, *shape, generator=gb, device=device, dtype=torch.float32)
+
+        out["x"][sl] = randn(L, d_inner)
+        out["dt"][sl] = F.softplus(randn(L, d_inner) - 2.0)
+        out["B"][sl] = randn(L, d_state)
+        out["C"][sl] = randn(L, d_state)
+        out["dy"][sl] = randn(L, d_inner)
+    out["A_log"] = A_log
+    return out
+
+
 def slot_inputs(F=128, N=32, M=196, D=384, seed=0, device="cpu"):
     """Config 2: inputs (F, M, D) = LayerNorm(N(0,1)); initial slots
     mu + |sigma| * eps with mu, sigma ~ N(0, 0.1) per dim and eps ~ N(0,1);

@@ -215,16 +215,68 @@ int hclsm_event_detect(const float* probs, const float* threshold, int32_t B, in
                        int32_t* pos, int32_t* counts, int32_t* meta, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Training-mode backward of the slot-attention iteration and of the Level-1
+ * event transformer (the gradients autograd takes through
+ * hclsm/objects/dynamic_slots.py:98-131 _iteration_step and
+ * hclsm/dynamics/level1_event.py:17-133, EventTransformerBlock / SwiGLUFFN).
+ * The weight-product gradients are library GEMMs; these are the stages between
+ * them.  All fp32 unless a dtype code says otherwise.
+ *
+ *   hclsm_colsum: out[c] = sum_r a[r, c] (deterministic two-stage sum; the
+ *     bias gradients of nn.Linear / nn.GRUCell).  Workspace
+ *     hclsm_colsum_workspace_size(C) bytes.
+ *   hclsm_layernorm_bwd: nn.LayerNorm backward from x and dy (statistics
+ *     recomputed as hclsm_layernorm forms them): dx (written, or added when
+ *     accumulate != 0), dw / db (may be NULL).  Workspace
+ *     hclsm_layernorm_bwd_workspace_size(rows, D) bytes when dw or db is given.
+ *   hclsm_gru_cell_bwd: nn.GRUCell backward (gates r, z, n) from the forward's
+ *     pre-bias products gi, gh (rows, 3H), its biases and input state h:
+ *     d_gi, d_gh (rows, 3H) and dh = z * dh_new (the state's direct term).
+ *   hclsm_slot_softmax_bwd: softmax over the slot axis (dim=1 of (F, N, M))
+ *     with the +-clamp logit clamp, recomputed from dots = q k^T (unscaled):
+ *     writes attn and d_dots = d(q k^T), both in dtype.
+ *   hclsm_residual_clamp_bwd: dpre = dout where -c <= (h + m) + b <= c.
+ *   hclsm_relu_bwd: dx = dy where y > 0 (y the ReLU output).
+ *   hclsm_swiglu_bwd: du (rows, 2C) of y = silu(u[:, :C]) * u[:, C:].
+ *   hclsm_event_mha_bwd: nn.MultiheadAttention core backward per (frame,
+ *     head), recomputing the probabilities from qkv (frames * T, 3E) and
+ *     key_pad; dout (frames * T, E) fp32; dqkv (frames * T, 3E) in dtype.
+ * ------------------------------------------------------------------------- */
+size_t hclsm_colsum_workspace_size(int32_t C);
+int hclsm_colsum(const float* a, float* out, int64_t rows, int32_t C, void* workspace, size_t workspace_bytes,
+                 void* stream);
+size_t hclsm_layernorm_bwd_workspace_size(int64_t rows, int32_t D);
+int hclsm_layernorm_bwd(const float* x, const float* w, const float* dy, float* dx, float* dw, float* db, int64_t rows,
+                        int32_t D, float eps, int32_t accumulate, void* workspace, size_t workspace_bytes,
+                        void* stream);
+int hclsm_gru_cell_bwd(const float* gi, const float* gh, const float* b_ih, const float* b_hh, const float* h,
+                       const float* dh_new, float* d_gi, float* d_gh, float* dh, int64_t rows, int32_t H,
+                       void* stream);
+int hclsm_slot_softmax_bwd(const float* dots, const float* d_attn, void* attn, void* d_dots, int32_t F, int32_t N,
+                           int32_t M, float scale, float clamp, float eps, int32_t dtype, void* stream);
+int hclsm_residual_clamp_bwd(const float* h, const float* m, const float* b, const float* dout, float* dpre,
+                             int64_t rows, int32_t C, float clamp, void* stream);
+int hclsm_relu_bwd(const void* y, int32_t y_dtype, const float* dy, void* dx, int32_t dx_dtype, int64_t n,
+                   void* stream);
+int hclsm_swiglu_bwd(const float* u, const float* ds, void* du, int64_t rows, int32_t C, int32_t out_dtype,
+                     void* stream);
+int hclsm_event_mha_bwd(const void* qkv, const uint8_t* key_pad, const float* dout, void* dqkv, int32_t frames,
+                        int32_t T, int32_t H, int32_t HD, float scale, int32_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Selective SSM scan, backward, without a caller workspace.
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory when they run the backward (host callbacks, allocator
  * hooks, runtimes with a fixed memory plan).  Same arguments and outputs as
  * hclsm_ssm_scan_bwd minus the workspace; the scratch lives in a fixed device
  * array of hclsm_ssm_scan_bwd_noalloc_max_scratch() bytes (48 MiB) that every
- * GPU loading the library holds until exit.  Returns HCLSM_ERR_WORKSPACE when
- * the problem needs more scratch than that.  Calls on one device share the
- * array: calls that overlap on the GPU race.  The first call on a device
- * resolves the array's address; make it before any stream capture.
+ * GPU loading the library holds until exit.  Arguments are checked as
+ * hclsm_ssm_scan_bwd checks them (same status codes); a valid problem that
+ * needs more scratch than that returns HCLSM_ERR_WORKSPACE.  Calls on one
+ * device share the array: calls that overlap on the GPU race.  The array's
+ * address is resolved on the first call under each CUDA context (primary or
+ * caller-created; a device reset makes a new one) and cached per context;
+ * make that first call before any stream capture.
  * ------------------------------------------------------------------------- */
 size_t hclsm_ssm_scan_bwd_noalloc_max_scratch(void);
 int hclsm_ssm_scan_bwd_noalloc(const void* x, const void* dt, const float* A_log, const void* B,

@@ -124,7 +124,7 @@ def test_detector_tail_matches_reference_golden(case):
     """EventDetector's mask (event_detector.py:162-170) from the reference's
     own probabilities: bit-identical mask, gradient to the probabilities, and
     the attached compaction equals that of the mask."""
-    from hclsm_b200.kernels.sparse_event_attn import event_detect
+    from hclsm_b200.kernels.sparse_event_attn import _cached_compaction, event_detect
     g = np.load(DET_GOLD)
     probs = torch.from_numpy(g[f"{case}/probs"]).cuda().requires_grad_(True)
     thr = torch.tensor([float(g[f"{case}/thr"])], device="cuda")
@@ -132,7 +132,7 @@ def test_detector_tail_matches_reference_golden(case):
     assert torch.equal(mask.detach().cpu(), torch.from_numpy(g[f"{case}/mask"]))
     (mask * torch.from_numpy(g[f"{case}/w"]).cuda()).sum().backward()
     assert torch.equal(probs.grad.cpu(), torch.from_numpy(g[f"{case}/dprobs"]))
-    idx, pos, counts, meta = mask._hclsm_events
+    idx, pos, counts, meta = _cached_compaction(mask)
     ref = event_compact(mask.detach())
     n = int(ref[3][0])
     assert int(meta[0]) == n and int(meta[1]) == int(ref[3][1])
@@ -142,7 +142,7 @@ def test_detector_tail_matches_reference_golden(case):
 @pytest.mark.parametrize("B,T,empty_rows", [(8, 64, []), (8, 64, [3]), (5, 300, [0, 4]), (3, 7, [0, 1, 2]),
                                             (1200, 3, [7])])
 def test_detector_tail_vs_torch(B, T, empty_rows):
-    from hclsm_b200.kernels.sparse_event_attn import event_detect
+    from hclsm_b200.kernels.sparse_event_attn import _cached_compaction, event_detect
     gen = torch.Generator().manual_seed(B * T)
     probs = torch.rand(B, T, generator=gen)
     for r in empty_rows:
@@ -157,7 +157,7 @@ def test_detector_tail_vs_torch(B, T, empty_rows):
     (mask * w).sum().backward()
     (ref * w).sum().backward()
     assert torch.equal(probs.grad, p2.grad)
-    idx, pos, counts, meta = mask._hclsm_events
+    idx, pos, counts, meta = _cached_compaction(mask)
     assert int(meta[2]) == (1 if empty_rows else 0)
     nz = torch.nonzero(ref.detach().reshape(-1) > 0.5).flatten()
     assert int(meta[0]) == len(nz) and torch.equal(idx[: len(nz)].long(), nz)
@@ -185,6 +185,15 @@ def test_gather_scatter_use_the_detector_compaction():
         s1 = scatter(None, states, upd, mask)
         s2 = scatter(None, states, upd, plain)
         assert torch.equal(s1, s2)
+        # an in-place edit of the mask after the detector drops the attached
+        # compaction: gather and scatter follow the edited mask
+        mask[1, :] = 1.0
+        plain[1, :] = 1.0
+        e3, p3, k3 = gather(None, states, mask)
+        e4, p4, k4 = gather(None, states, plain)
+        assert k3 == k4 == 20 and torch.equal(e3, e4) and torch.equal(p3, p4)
+        upd = torch.randn(e3.shape, generator=gen).cuda()
+        assert torch.equal(scatter(None, states, upd, mask), scatter(None, states, upd, plain))
 
 
 def _mha_call(qkv, kp, frames, T, H, HD, scale):

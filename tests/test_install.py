@@ -104,9 +104,9 @@ def test_patched_ssm_block_matches_reference_golden():
     y = inst._ssm_block_forward(blk, x)
     assert rel_err(y.detach().cpu().numpy(), g["blk/y"]) < 1e-5
     y.backward(torch.from_numpy(g["blk/dy"]).cuda())
-    assert rel_err(x.grad.cpu().numpy(), g["blk/dx"]) < 1e-4
+    assert rel_err(x.grad.cpu().numpy(), g["blk/dx"]) < 1e-5
     for name, p in blk.named_parameters():
-        assert rel_err(p.grad.cpu().numpy(), g[f"blk/g/{name}"]) < 1e-4, name
+        assert rel_err(p.grad.cpu().numpy(), g[f"blk/g/{name}"]) < 1e-5, name
 
 
 class _DSA(nn.Module):
@@ -136,4 +136,48 @@ def test_patched_iteration_step_matches_reference_golden():
     with torch.no_grad():
         for i in range(3):
             s = step(m, s, k, v)
-    assert rel_err(s.cpu().numpy(), g["iter/slots3"]) < 2e-2
+    assert s.dtype == torch.float32
+    assert rel_err(s.cpu().numpy(), g["iter/slots3"]) < 1e-5  # fp32 module and inputs: fp32 arithmetic
+
+
+REF = os.environ.get("HCLSM_REFERENCE", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "hclsm")), reason="reference source tree not present")
+def test_install_on_the_real_reference_package():
+    """install() on the reference package itself (imported from its source
+    tree, CPU only, no compute): every documented call site is replaced by this
+    library's function, and uninstall() restores the reference's own."""
+    import importlib
+    import sys
+
+    sys.path.insert(0, REF)
+    try:
+        hclsm = importlib.import_module("hclsm")
+        importlib.import_module("hclsm.kernels")
+        l0 = importlib.import_module("hclsm.dynamics.level0_ssm")
+        ds = importlib.import_module("hclsm.objects.dynamic_slots")
+        hm = importlib.import_module("hclsm.dynamics.hierarchy_manager")
+        l1 = importlib.import_module("hclsm.dynamics.level1_event")
+        ed = importlib.import_module("hclsm.dynamics.event_detector")
+        before = {(c, n): getattr(c, n) for c, n in (
+            (l0.SimplifiedSSMBlock, "forward"), (l0.Level0SSM, "forward"),
+            (ds.DynamicSlotAttention, "_iteration_step"), (ds.DynamicSlotAttention, "forward"),
+            (hm.HierarchyManager, "gather_events"), (hm.HierarchyManager, "scatter_events"),
+            (l1.Level1EventDynamics, "forward"), (ed.EventDetector, "forward"))}
+        done = inst.install(hclsm)
+        try:
+            assert len(done) == 14, done
+            assert hclsm.kernels.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
+            assert hclsm.kernels.ssm_scan_kernel.ssm_scan_fn is hclsm_b200.kernels.ssm_scan_fn
+            assert hclsm.kernels.slot_attention_fn is hclsm_b200.kernels.slot_attention_fn
+            assert hclsm.kernels.sparse_event_attn_fn is hclsm_b200.kernels.sparse_event_attn_fn
+            for (c, n), f in before.items():
+                assert getattr(c, n) is not f, (c.__name__, n)
+            assert l0.SimplifiedSSMBlock.forward is inst._ssm_block_forward
+        finally:
+            inst.uninstall()
+        for (c, n), f in before.items():
+            assert getattr(c, n) is f
+    finally:
+        sys.path.remove(REF)

@@ -85,7 +85,7 @@ def test_fwd_bwd_vs_oracle(dtype, shape, gated):
     for name, got in zip(names, grads):
         if got is None:
             continue
-        tol = TOL[dtype] if dtype == torch.bfloat16 else 2e-5
+        tol = TOL[dtype] if dtype == torch.bfloat16 else 1e-5
         assert rel_err(_np(got), gr[name]) < tol, (name, rel_err(_np(got), gr[name]))
 
 
@@ -180,7 +180,7 @@ def test_bwd_any_state_and_length(dtype, shape):
         grads = scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], d["D"], d["z"], clamp=clamp)
         gr = oscan.scan_bwd(o["x"], o["dt"], o["A_log"], o["B"], o["C"], o["dy"], o["D"], o["z"], clamp=clamp)
         for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC", "dD", "dz"), grads):
-            tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
+            tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
             assert rel_err(_np(got), gr[name]) < tol, (name, clamp, rel_err(_np(got), gr[name]))
 
 
@@ -239,7 +239,7 @@ def test_dt_softplus_vs_oracle(dtype, shape, clamp):
     assert rel_err(_np(y), yr) < TOL[dtype]
     gr = oscan.scan_bwd(o["x"], dt_eff, o["A_log"], o["B"], o["C"], o["dy"], clamp=clamp)
     gr["ddt"] = gr["ddt"] * torch.sigmoid(raw64).numpy()
-    tol = TOL[dtype] if dtype == torch.bfloat16 else 2e-5
+    tol = TOL[dtype] if dtype == torch.bfloat16 else 1e-5
     for name, got in zip(("dx", "ddt", "dA_log", "dB", "dC"), grads):
         assert rel_err(_np(got), gr[name]) < tol, (name, rel_err(_np(got), gr[name]))
     if dtype == torch.bfloat16 and S == 16 and Dn % 2 == 0:

@@ -63,14 +63,17 @@ def test_core_backward_matches_autograd():
         assert rel_err(_np(x.grad), _np(y.grad)) < 1e-4
 
 
-def test_iterations_golden():
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
+def test_iterations_golden(dtype, tol):
+    """fp32: every weight product in fp32 (the reference without autocast);
+    bf16: bf16 operands, fp32 accumulation (the reference under autocast)."""
     g = np.load(GOLD)
     W = {k[len("iter/w/"):]: torch.from_numpy(g[k]) for k in g.files if k.startswith("iter/w/")}
-    p = SlotIterationParams.from_state(W, "cuda")
+    p = SlotIterationParams.from_state(W, "cuda", dtype=dtype)
     k, v = (torch.from_numpy(g[f"iter/{n}"]).cuda() for n in ("k", "v"))
     s = torch.from_numpy(g["iter/slots0"]).cuda()
     out = slot_attention_iterations(s, k, v, p, 3)
-    assert rel_err(_np(out), g["iter/slots3"]) < 2e-2
+    assert rel_err(_np(out), g["iter/slots3"]) < tol
 
 
 def test_config2_three_iterations_vs_oracle():
@@ -88,3 +91,22 @@ def test_config2_three_iterations_vs_oracle():
     for _ in range(3):
         s = osl.iteration_step(s, k.float().numpy(), v.float().numpy(), Wn)
     assert rel_err(_np(out), s) < 2e-2
+
+
+@pytest.mark.parametrize("shape", [(128, 32, 196, 384), (3, 5, 33, 128), (2, 64, 130, 256)])
+def test_core_tcgen05_and_mma_agree_with_oracle(shape, monkeypatch):
+    """Shapes the tcgen05 core covers, run once on it and once on the
+    mma.sync core (HCLSM_SLOT_CORE=mma forces that one): both against the
+    oracle at 2e-2 (bf16 operands, fp32 accumulation)."""
+    B, N, M, D = shape
+    gen = torch.Generator().manual_seed(sum(shape) + 1)
+    Q, K, V = (torch.randn(B, n, D, generator=gen).to(torch.bfloat16) for n in (N, M, M))
+    ro, ra = osl.naive_slot_attention(Q.float().numpy(), K.float().numpy(), V.float().numpy())
+    for sel in ("tc", "mma"):
+        if sel == "mma":
+            monkeypatch.setenv("HCLSM_SLOT_CORE", "mma")
+        else:
+            monkeypatch.delenv("HCLSM_SLOT_CORE", raising=False)
+        out, attn = slot_attention_core(Q.cuda(), K.cuda(), V.cuda(), attn_fp32=True)
+        assert rel_err(_np(out), ro) < 2e-2, sel
+        assert rel_err(_np(attn), ra) < 2e-2, sel
