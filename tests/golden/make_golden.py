@@ -317,10 +317,209 @@ def event_cases():
     return out
 
 
+def train_cases():
+    """Training-mode fixtures (fp32, CPU): gradients the reference's autograd
+    takes through (a) three DynamicSlotAttention._iteration_step calls
+    (hclsm/objects/dynamic_slots.py:98-131) w.r.t. the initial slots, k, v and
+    every parameter, with inputs that make the +-30 logit clamp and the +-50
+    state clamp bind; (b) DynamicSlotAttention.forward (:133-203) with fixed
+    initial slots, loss on slots and existence; (c) the model's event path
+    HierarchyManager.gather_events -> Level1EventDynamics(ev, pad, alive) ->
+    scatter_events (hierarchy_manager.py:42-118, level1_event.py:85-133).
+    Each loss is sum(output * w) with a fixed random w."""
+    from hclsm.config import Level1Config, ObjectConfig
+    from hclsm.dynamics.hierarchy_manager import HierarchyManager
+    from hclsm.dynamics.level1_event import Level1EventDynamics
+    from hclsm.objects.dynamic_slots import DynamicSlotAttention
+
+    out = {}
+    # (a) iterations
+    g = torch.Generator().manual_seed(1100)
+    F_, N, M, D = 3, 8, 49, 64
+    mod = DynamicSlotAttention(ObjectConfig(d_slot=D, n_max_slots=N, n_iterations=3), d_input=D)
+    with torch.no_grad():
+        for name, p in mod.named_parameters():
+            if "norm" in name:
+                p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g) if name.endswith("weight")
+                        else 0.1 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+    slots = torch.randn(F_, N, D, generator=g)
+    slots[0, 1, :5] = 70.0  # past the +-50 clamp
+    slots[1, 2, 3:9] = -65.0
+    k = torch.randn(F_, M, D, generator=g)
+    v = torch.randn(F_, M, D, generator=g)
+    k[2, 7] *= 40.0  # logits past +-30
+    w = torch.randn(F_, N, D, generator=g)
+    leaves = [t.clone().requires_grad_(True) for t in (slots, k, v)]
+    s = leaves[0]
+    for _ in range(3):
+        s = mod._iteration_step(s, leaves[1], leaves[2])
+    (s * w).sum().backward()
+    out.update({"it/slots0": _np(slots), "it/k": _np(k), "it/v": _np(v), "it/w": _np(w), "it/slots3": _np(s),
+                "it/dslots": _np(leaves[0].grad), "it/dk": _np(leaves[1].grad), "it/dv": _np(leaves[2].grad)})
+    for name, p in mod.named_parameters():
+        out[f"it/p/{name}"] = _np(p)
+        if p.grad is not None:
+            out[f"it/g/{name}"] = _np(p.grad)
+    # (b) the whole forward, differentiable
+    g = torch.Generator().manual_seed(1200)
+    cfg = ObjectConfig(d_slot=32, n_max_slots=6, n_iterations=3, existence_threshold=0.5, birth_threshold=0.7)
+    mod = DynamicSlotAttention(cfg, d_input=24)
+    with torch.no_grad():
+        for name, p in mod.named_parameters():
+            if "norm" in name:
+                continue
+            p.copy_(torch.randn(p.shape, generator=g) * 0.2)
+    slots0 = torch.randn(3, 6, 32, generator=g) * 0.5
+    mod._init_slots = lambda B, device, s0=slots0: s0.clone()
+    inputs = torch.randn(3, 10, 24, generator=g, requires_grad=True)
+    ws = torch.randn(3, 6, 32, generator=g)
+    wa = torch.randn(3, 6, generator=g)
+    sl, alive = mod(inputs)
+    ((sl * ws).sum() + (alive * wa).sum()).backward()
+    out.update({"dsa/inputs": _np(inputs), "dsa/slots0": _np(slots0), "dsa/ws": _np(ws), "dsa/wa": _np(wa),
+                "dsa/slots": _np(sl), "dsa/alive": _np(alive), "dsa/dinputs": _np(inputs.grad)})
+    for name, p in mod.named_parameters():
+        out[f"dsa/p/{name}"] = _np(p)
+        if p.grad is not None:
+            out[f"dsa/g/{name}"] = _np(p.grad)
+    # (c) the event path of the model
+    g = torch.Generator().manual_seed(1300)
+    Bn, T, N, D = 3, 10, 6, 64
+    l1 = Level1EventDynamics(Level1Config(d_model=64, n_layers=2, n_heads=4), d_slot=D)
+    with torch.no_grad():
+        for name, p in l1.named_parameters():
+            if "norm" in name:
+                p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g) if name.endswith("weight")
+                        else 0.1 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+    states = torch.randn(Bn, T, N, D, generator=g, requires_grad=True)
+    mask = (torch.rand(Bn, T, generator=g) < 0.3).float()
+    mask[2] = 0.0
+    mask[2, 0] = 1.0
+    alive = torch.ones(Bn, N)
+    alive[1, 4:] = 0.0
+    wy = torch.randn(Bn, T, N, D, generator=g)
+    hm = HierarchyManager(D, 32)
+    ev, pad, kmax = hm.gather_events(states, mask)
+    upd = l1(ev, pad, alive)
+    y = hm.scatter_events(states, upd, mask)
+    (y * wy).sum().backward()
+    out.update({"ev/states": _np(states), "ev/mask": _np(mask), "ev/alive": _np(alive), "ev/wy": _np(wy),
+                "ev/y": _np(y), "ev/dstates": _np(states.grad), "ev/n_heads": np.array(4), "ev/n_layers": np.array(2)})
+    for name, p in l1.named_parameters():
+        out[f"ev/p/{name}"] = _np(p)
+        out[f"ev/g/{name}"] = _np(p.grad)
+    return out
+
+
+def model_cases():
+    """The tiny-preset HCLSMWorldModel (hclsm/model.py:200-412) run forward and
+    backward on CPU in fp32 (loss = sum(final_prediction * w)).  Recorded at
+    every hot-path call site: the inputs, outputs and upstream gradients of
+    DynamicSlotAttention (with the initial slots its _init_slots drew),
+    Level0SSM, the EventDetector's decision, HierarchyManager.gather_events,
+    Level1EventDynamics and HierarchyManager.scatter_events, plus the
+    parameter gradients of those modules.  Their weights come from name-seeded
+    generators (model_weights.py), so the fixture stores none."""
+    from hclsm.config import HCLSMConfig
+    from hclsm.model import HCLSMWorldModel
+
+    sys.path.insert(0, HERE)
+    from model_weights import grad_sample, load_seeded
+
+    torch.manual_seed(1400)
+    model = HCLSMWorldModel(HCLSMConfig.tiny())
+    model.eval()
+    load_seeded("sa", model.slot_attention)
+    load_seeded("l0", model.level0_ssm)
+    load_seeded("l1", model.level1_event)
+    rec = {}
+
+    def keep(name, t):
+        rec[name] = t
+        if t.requires_grad:
+            t.register_hook(lambda g, n=name: rec.__setitem__(n + "/grad", g))
+
+    sa, l0, ed, l1, hm = (model.slot_attention, model.level0_ssm, model.event_detector, model.level1_event,
+                          model.hierarchy_manager)
+    f_init, f_sa, f_l0, f_ed, f_l1 = sa._init_slots, sa.forward, l0.forward, ed.forward, l1.forward
+    f_g, f_s = hm.gather_events, hm.scatter_events
+
+    def init_slots(B, device):
+        s0 = f_init(B, device)
+        rec["sa/slots0"] = s0.detach().clone()
+        return s0
+
+    def sa_fwd(inputs, return_attention=False):
+        keep("sa/inputs", inputs)
+        slots, alive = f_sa(inputs)
+        keep("sa/slots", slots)
+        keep("sa/alive", alive)
+        return slots, alive
+
+    def l0_fwd(obj_states, obj_mask=None):
+        keep("l0/x", obj_states)
+        rec["l0/mask"] = obj_mask
+        y = f_l0(obj_states, obj_mask)
+        keep("l0/y", y)
+        return y
+
+    def ed_fwd(states):
+        probs, mask = f_ed(states)
+        rec["ed/probs"] = probs.detach()
+        rec["ed/mask"] = mask.detach()
+        return probs, mask
+
+    def gather(states, event_mask):
+        keep("g/states", states)
+        rec["g/mask"] = event_mask.detach()
+        ev, pad, k = f_g(states, event_mask)
+        keep("g/ev", ev)
+        rec["g/pad"] = pad
+        return ev, pad, k
+
+    def l1_fwd(ev, pad=None, obj_mask=None):
+        keep("l1/x", ev)
+        rec["l1/pad"] = pad
+        rec["l1/obj_mask"] = obj_mask
+        y = f_l1(ev, pad, obj_mask)
+        keep("l1/y", y)
+        return y
+
+    def scatter(base, upd, event_mask):
+        keep("s/base", base)
+        keep("s/upd", upd)
+        y = f_s(base, upd, event_mask)
+        keep("s/y", y)
+        return y
+
+    sa._init_slots, sa.forward, l0.forward, ed.forward, l1.forward = init_slots, sa_fwd, l0_fwd, ed_fwd, l1_fwd
+    hm.gather_events, hm.scatter_events = gather, scatter
+    g = torch.Generator().manual_seed(1401)
+    video = torch.rand(2, 3, 3, 224, 224, generator=g)
+    out = model(video)
+    w = torch.randn(out.predicted_states.shape, generator=g)
+    (out.predicted_states * w).sum().backward()
+    res = {"m/w": _np(w), "m/pred": _np(out.predicted_states)}
+    for k, v in rec.items():
+        if v is not None:
+            res[f"m/{k}"] = _np(v)
+    for prefix, mod in (("sa", sa), ("l0", l0), ("l1", l1)):
+        for name, p in mod.named_parameters():
+            if p.grad is not None:
+                res[f"m/{prefix}/g/{name}"] = _np(grad_sample(name, p.grad))
+    res["m/ed/thr"] = _np(ed.learned_threshold.reshape(1))
+    res["m/n_heads"] = np.array(model.level1_event.blocks[0].attn.num_heads)
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", default=None, help="write only this fixture (level0, dsa, detector)")
+    ap.add_argument("--only", default=None, help="write only this fixture (level0, dsa, detector, train, model)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(1)
@@ -332,6 +531,14 @@ def main():
         np.savez_compressed(os.path.join(HERE, "detector_golden.npz"), **detector_cases())
         print("wrote detector_golden.npz")
         return
+    if args.only == "model":
+        np.savez_compressed(os.path.join(HERE, "model_golden.npz"), **model_cases())
+        print("wrote model_golden.npz")
+        return
+    if args.only == "train":
+        np.savez_compressed(os.path.join(HERE, "train_golden.npz"), **train_cases())
+        print("wrote train_golden.npz")
+        return
     if args.only == "dsa":
         np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
         print("wrote dsa_golden.npz")
@@ -342,6 +549,8 @@ def main():
     np.savez_compressed(os.path.join(HERE, "level0_golden.npz"), **level0_cases())
     np.savez_compressed(os.path.join(HERE, "dsa_golden.npz"), **dsa_cases())
     np.savez_compressed(os.path.join(HERE, "detector_golden.npz"), **detector_cases())
+    np.savez_compressed(os.path.join(HERE, "train_golden.npz"), **train_cases())
+    np.savez_compressed(os.path.join(HERE, "model_golden.npz"), **model_cases())
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 
