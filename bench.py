@@ -711,6 +711,37 @@ def run_event(args, rank, world, dev, peaks, flush):
     return leg
 
 
+def run_ssm_block(args, rank, world, dev, flush):
+    """SimplifiedSSMBlock forward + backward through install()'s patched
+    forward (LayerNorm, the five projections as library GEMMs, softplus(dt) + clamp +
+    scan + SiLU gate in one kernel, out_proj, residual) under bf16 autocast, on
+    config-1 scan shapes: 256 sequences x T=64, d_model 384 (d_inner 768),
+    d_state 16."""
+    import torch
+
+    from hclsm_b200.install import _ssm_block_forward
+    from hclsm_b200.workloads import ssm_block_inputs
+
+    blk, x = ssm_block_inputs(seed=30, device=dev)
+    x.requires_grad_(True)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = _ssm_block_forward(blk, x)
+        y.float().sum().backward()
+
+    for _ in range(max(args.warmup, 5)):
+        step()
+    torch.cuda.synchronize(dev)
+    ms = _timed(step, 20, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    return {"metric": "ssm_block_fwd_bwd_sequences_per_s", "value": x.shape[0] / (ms * 1e-3),
+            "unit": "sequences/s", "ms_per_step": ms,
+            "config": "SimplifiedSSMBlock fwd+bwd, 256 sequences x T=64 x d_model 384 (d_inner 768, d_state 16), "
+                      "bf16 autocast, softplus(dt) fused into the scan; per rank; "
+                      "L2 flushed between steps"}
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -763,6 +794,7 @@ def main():
         legs["config1"] = run_config1(args, rank, world, dev, peaks, flush)
         legs["config2_slot_attention"] = run_slot(args, rank, world, dev, peaks, flush)
         legs["config3_event_attention"] = run_event(args, rank, world, dev, peaks, flush)
+        legs["ssm_block"] = run_ssm_block(args, rank, world, dev, flush)
         del flush
     cpu = None
     if rank == 0 and not args.no_cpu:
