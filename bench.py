@@ -11,8 +11,8 @@ attention), each with its roofline and a CPU baseline.
 
 N>1 runs under torchrun, one process per GPU over NCCL.  The scan needs no
 collective on its data path (sequences are independent); after the timed
-region NCCL all-gathers every rank's outputs to rank 0, which checks them bit
-for bit against its own run of the same sequences, and all-reduces dA_log.
+region NCCL gathers every rank's outputs to rank 0, which checks them bit for
+bit against its own run of the same shards, and all-reduces dA_log.
 
 Output: one JSON line on rank 0.
 """
@@ -306,12 +306,13 @@ def run_config4(args, rank, world, dev):
 
 
 def verify_config4(args, rank, world, dev, shard, y, grads, d):
-    """Outside the timed region.  N > 1: NCCL all-gathers y, dx, ddt, dB, dC of
-    every rank in rounds of 64 sequences per rank and all-reduces dA_log; rank
-    0 recomputes each gathered round on its own GPU (the same kernels on the
-    same regenerated sequences) and requires bit equality, and dA_log within
-    1e-5 (its sum over sequences runs in another order).  Every N: the first
-    16 sequences against the CPU oracle at 2e-2 (bf16 I/O)."""
+    """Outside the timed region.  N > 1: rank 0 reruns every rank's shard on
+    its own GPU (the same regenerated sequences, the same call size and path),
+    NCCL gathers each rank's y, dx, ddt, dB, dC to rank 0 in rounds of 64
+    sequences, and rank 0 requires bit equality; dA_log is all-reduced and
+    compared with rank 0's sum of the rerun shards at 1e-5 (the two sums run
+    in different orders).  Every N: the first 16 sequences against the CPU
+    oracle at 2e-2 (bf16 I/O)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -325,37 +326,41 @@ def verify_config4(args, rank, world, dev, shard, y, grads, d):
     mine = dict(zip(names, (y, grads[0], grads[1], grads[3], grads[4])))
     dA = grads[2].clone()
     if world > 1:
+        from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, states_bytes
+
         blk = 64
         ranges = [tuple(64 * v for v in shard_range(args.seqs // 64, r, world)) for r in range(world)]
-        rounds = max((e - s) // blk for s, e in ranges)
         exact = True
-        for j in range(rounds):
-            gathered = {}
-            for k in names:
-                src = mine[k]
-                part = src[j * blk:(j + 1) * blk] if (j + 1) * blk <= src.shape[0] else torch.zeros_like(src[:blk])
-                buf = torch.empty((world * blk,) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
-                dist.all_gather_into_tensor(buf, part.contiguous())
-                gathered[k] = buf
+        tot = torch.zeros_like(dA) if rank == 0 else None
+        for r, (s, e) in enumerate(ranges):
+            n = e - s
+            ref = None
             if rank == 0:
-                for r, (s, e) in enumerate(ranges):
-                    if s + (j + 1) * blk > e:
-                        continue
-                    dd = scan_inputs_range(s + j * blk, blk, L, DI, DS, dtype=torch.bfloat16, seed=SEED, device=dev)
-                    yr = scan_fwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"])
-                    gr = scan_bwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], dd["dy"])
-                    ref = dict(zip(names, (yr, gr[0], gr[1], gr[3], gr[4])))
-                    for k in names:
-                        exact &= bool(torch.equal(gathered[k][r * blk:(r + 1) * blk], ref[k]))
-            del gathered
+                # rank r's shard again on this GPU: same sequences, same call
+                # size (the kernels' work split depends on it), same path
+                dd = scan_inputs_range(s, n, L, DI, DS, dtype=torch.bfloat16, seed=SEED, device=dev)
+                st = torch.empty(states_bytes(n, L, DI, DS, torch.bfloat16), dtype=torch.uint8, device=dev)
+                ws = torch.empty(bwd_workspace_bytes(n, L, DI, DS), dtype=torch.uint8, device=dev)
+                yr = scan_fwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], states=st)
+                gr = scan_bwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], dd["dy"], workspace=ws, states=st)
+                ref = dict(zip(names, (yr, gr[0], gr[1], gr[3], gr[4])))
+                tot += gr[2]
+                del dd, st, ws
+            # NCCL carries rank r's outputs to rank 0 in rounds of 64 sequences
+            for j in range(n // blk):
+                for k in names:
+                    if rank == r and r != 0:
+                        dist.send(mine[k][j * blk:(j + 1) * blk].contiguous(), dst=0)
+                    elif rank == 0:
+                        if r == 0:
+                            got = mine[k][j * blk:(j + 1) * blk]
+                        else:
+                            got = torch.empty((blk,) + tuple(mine[k].shape[1:]), dtype=mine[k].dtype, device=dev)
+                            dist.recv(got, src=r)
+                        exact &= bool(torch.equal(got, ref[k][j * blk:(j + 1) * blk]))
+            del ref
         dist.all_reduce(dA)
-        # the single-GPU dA_log of the whole job, accumulated round by round on rank 0
         if rank == 0:
-            tot = torch.zeros_like(dA)
-            for s in range(0, args.seqs, 1024):
-                dd = scan_inputs_range(s, min(1024, args.seqs - s), L, DI, DS, dtype=torch.bfloat16, seed=SEED,
-                                       device=dev)
-                tot += scan_bwd_raw(dd["x"], dd["dt"], dd["A_log"], dd["B"], dd["C"], dd["dy"])[2]
             rel = float((dA - tot).abs().max() / tot.abs().max())
             out.update({"gathered_bit_identical": exact, "dA_log_rel_err": rel})
     if rank == 0 and shard[0] == 0:

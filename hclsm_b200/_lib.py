@@ -56,6 +56,8 @@ SIGNATURES = {
     "hclsm_event_scatter": (ctypes.c_int, [_vp] * 5 + [_i64, _i64, _i32, _i32, _i32, _vp]),
     "hclsm_event_mha": (ctypes.c_int, [_vp] * 3 + [_i32] * 4 + [ctypes.c_float, _i32, _vp]),
     "hclsm_swiglu": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _vp]),
+    "hclsm_gru_cell_ln": (ctypes.c_int, [_vp] * 9 + [_i32, _i64, _i32, ctypes.c_float, _vp]),
+    "hclsm_residual_clamp_ln": (ctypes.c_int, [_vp] * 8 + [_i32, _i64, _i32, ctypes.c_float, ctypes.c_float, _vp]),
     "hclsm_colsum_workspace_size": (_sz, [_i32]),
     "hclsm_colsum": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _sz, _vp]),
     "hclsm_layernorm_bwd_workspace_size": (_sz, [_i64, _i32]),

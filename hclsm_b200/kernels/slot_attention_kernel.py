@@ -32,8 +32,9 @@ def _c(t):
     return t
 
 
-def slot_attention_core(Q, K, V, scale=None, *, clamp=0.0, eps=0.0, return_attn=True, attn_fp32=None):
-    """Forward only.  Q (F, N, D), K/V (F, M, D) on CUDA, fp32 or bf16."""
+def slot_attention_core(Q, K, V, scale=None, *, clamp=0.0, eps=0.0, return_attn=True, attn_fp32=None, out=None):
+    """Forward only.  Q (F, N, D), K/V (F, M, D) on CUDA, fp32 or bf16.  ``out``
+    (optional): a contiguous (F, N, D) tensor of the I/O dtype to write into."""
     _lib.require_cuda(Q, K, V)
     if Q.dim() != 3 or K.dim() != 3 or V.shape != K.shape or Q.shape[0] != K.shape[0] or Q.shape[2] != K.shape[2]:
         raise ValueError("expected Q (B, N, D) and K, V (B, M, D)")
@@ -43,7 +44,10 @@ def slot_attention_core(Q, K, V, scale=None, *, clamp=0.0, eps=0.0, return_attn=
     M = K.shape[1]
     if scale is None:
         scale = D ** -0.5
-    out = torch.empty(F, N, D, dtype=dt, device=Q.device)
+    if out is None:
+        out = torch.empty(F, N, D, dtype=dt, device=Q.device)
+    elif out.shape != (F, N, D) or out.dtype != dt or not out.is_contiguous() or out.data_ptr() % 16:
+        raise ValueError("out must be a contiguous, 16-byte aligned (F, N, D) tensor of the I/O dtype")
     if attn_fp32 is None:
         attn_fp32 = dt == torch.float32
     attn = None
@@ -133,6 +137,32 @@ def residual_clamp(h, m, b, clamp=50.0, out=None, out_bf16=None):
     return out
 
 
+def gru_cell_ln(gi, gh, b_ih, b_hh, h, ln_w, ln_b, ln_dtype, eps=1e-5):
+    """(GRUCell state fp32, LayerNorm of it in ln_dtype) in one pass."""
+    H = h.shape[-1]
+    rows = h.numel() // H
+    out = torch.empty_like(h)
+    ln = torch.empty(h.shape, dtype=ln_dtype, device=h.device)
+    rc = _lib.load().hclsm_gru_cell_ln(_lib.ptr(gi), _lib.ptr(gh), _lib.ptr(b_ih), _lib.ptr(b_hh), _lib.ptr(h),
+                                       _lib.ptr(out), _lib.ptr(ln_w), _lib.ptr(ln_b), _lib.ptr(ln),
+                                       _lib.dtype_code(ln_dtype), rows, H, float(eps), _lib.stream_ptr(h.device))
+    _lib.check(rc, "hclsm_gru_cell_ln")
+    return out, ln
+
+
+def residual_clamp_ln(h, m, b, clamp, ln_w, ln_b, ln_dtype, out_bf16=None, eps=1e-5):
+    """(clamp(h + m + b) fp32, LayerNorm of it in ln_dtype) in one pass; the
+    optional bf16 copy of the first goes to out_bf16."""
+    C = h.shape[-1]
+    out = torch.empty_like(h)
+    ln = torch.empty(h.shape, dtype=ln_dtype, device=h.device)
+    rc = _lib.load().hclsm_residual_clamp_ln(_lib.ptr(h), _lib.ptr(m), _lib.ptr(b), _lib.ptr(out), _lib.ptr(out_bf16),
+                                             _lib.ptr(ln_w), _lib.ptr(ln_b), _lib.ptr(ln), _lib.dtype_code(ln_dtype),
+                                             h.numel() // C, C, float(clamp), float(eps), _lib.stream_ptr(h.device))
+    _lib.check(rc, "hclsm_residual_clamp_ln")
+    return out, ln
+
+
 # ---- the fused refinement step -------------------------------------------------------
 @dataclass
 class SlotIterationParams:
@@ -158,6 +188,7 @@ class SlotIterationParams:
     scale: float
     b1_bf16: torch.Tensor | None = None  # the MLP's first bias for the fused GEMM epilogue (bf16 path)
     dtype: torch.dtype = torch.bfloat16
+    w_gru_t: torch.Tensor | None = None  # (2, D, 3D): [W_ih^T, W_hh^T] for one batched product (bf16 path)
 
     @classmethod
     def from_state(cls, sd: dict, device, d_slot: int | None = None, dtype=torch.bfloat16):
@@ -176,7 +207,7 @@ class SlotIterationParams:
                    f("gru.bias_hh"), w("mlp.0.weight"), b1, w("mlp.2.weight"), f("mlp.2.bias"),
                    f("norm_pre_attn.weight"), f("norm_pre_attn.bias"), f("norm_slots.weight"),
                    f("norm_slots.bias"), D ** -0.5, b1.to(torch.bfloat16) if dtype == torch.bfloat16 else None,
-                   dtype)
+                   dtype, torch.stack([w("gru.weight_ih"), w("gru.weight_hh")]) if dtype == torch.bfloat16 else None)
 
     @classmethod
     def from_module(cls, mod, dtype=torch.bfloat16):
@@ -189,24 +220,51 @@ def _mm(a, w_t):
     return torch.mm(a, w_t, out_dtype=torch.float32)
 
 
-def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_lp=None):
+def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_lp=None, pair=None):
     """One _iteration_step (dynamic_slots.py:98-131).  slots (F, N, D) fp32 (the
     carried state), k and v (F, M, D) in ``p.dtype``.  Returns (slots_new fp32,
     a bf16 copy of it on the bf16 path, else None)."""
+    out, out_lp, _ = _iteration(slots, k, v, p, slots_lp, pair, None, False)
+    return out, out_lp
+
+
+def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_next_sn):
+    """The step with its row stages fused: LayerNorm (skipped when ``sn``, the
+    normalised slots, is given), W_q, the attention core, the GRU gate
+    products, GRUCell + norm_slots LayerNorm (one kernel), the MLP, and
+    residual + clamp (+ the next step's norm_pre_attn LayerNorm when
+    ``want_next_sn``; one kernel).  Returns (slots_new fp32, bf16 copy or None,
+    next sn or None).
+
+    bf16 path with ``pair`` (a (2, F*N, D) bf16 buffer whose [1] holds the
+    slots in bf16): the attention core writes its updates into pair[0], both
+    GRU gate products run as one batched GEMM over pair and the stacked
+    [W_ih^T, W_hh^T], and the new slots' bf16 copy lands in pair[1] for the
+    next iteration."""
     F, N, D = slots.shape
     R = F * N
     dt = p.dtype
     s2 = slots.reshape(R, D)
     lp = dt == torch.bfloat16
-    if lp and slots_lp is None:
+    if lp and slots_lp is None and pair is None:
         slots_lp = s2.to(torch.bfloat16)
-    sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=dt)
-    q = torch.mm(sn, p.wq_t).reshape(F, N, D)
-    upd, _ = slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False)
-    gi = _mm(upd.reshape(R, D), p.w_ih_t)
-    gh = _mm(slots_lp.reshape(R, D) if lp else s2, p.w_hh_t)
-    h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
-    m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=dt)
+    if sn is None:
+        sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=dt)
+    q = torch.mm(sn.reshape(R, D), p.wq_t).reshape(F, N, D)
+    if lp and pair is not None and p.w_gru_t is not None:
+        slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False, out=pair[0].view(F, N, D))
+        g2 = torch.bmm(pair, p.w_gru_t, out_dtype=torch.float32)
+        gi, gh = g2[0], g2[1]
+    else:
+        upd, _ = slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False)
+        gi = _mm(upd.reshape(R, D), p.w_ih_t)
+        gh = _mm(slots_lp.reshape(R, D) if lp else s2, p.w_hh_t)
+    fuse = D % 128 == 0 and D <= 1024  # the row-fused kernels' shapes
+    if fuse:
+        h, m = gru_cell_ln(gi, gh, p.b_ih, p.b_hh, s2, p.ln_mlp_w, p.ln_mlp_b, dt)
+    else:
+        h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
+        m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=dt)
     if lp and p.b1_bf16 is not None:
         # bias + ReLU in the library GEMM's epilogue, bf16 out (the MLP runs in
         # the autocast dtype in the reference)
@@ -216,16 +274,27 @@ def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_lp=None)
     else:
         m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
     m = _mm(m, p.w2_t)
-    out_lp = torch.empty(R, D, dtype=torch.bfloat16, device=slots.device) if lp else None
-    out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_lp)
-    return out.reshape(F, N, D), (out_lp.reshape(F, N, D) if lp else None)
+    if lp:
+        out_lp = pair[1] if pair is not None else torch.empty(R, D, dtype=torch.bfloat16, device=slots.device)
+    else:
+        out_lp = None
+    sn_next = None
+    if want_next_sn and fuse:
+        out, sn_next = residual_clamp_ln(h, m, p.b2, 50.0, p.ln_attn_w, p.ln_attn_b, dt, out_bf16=out_lp)
+    else:
+        out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_lp)
+    return out.reshape(F, N, D), (out_lp.reshape(F, N, D) if lp else None), sn_next
 
 
 def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations: int):
     s = slots.float().contiguous()
-    sl = None
     k = _c(k.to(p.dtype))
     v = _c(v.to(p.dtype))
-    for _ in range(n_iterations):
-        s, sl = slot_attention_iteration(s, k, v, p, sl)
+    F, N, D = s.shape
+    pair, sl, sn = None, None, None
+    if p.dtype == torch.bfloat16 and p.w_gru_t is not None and (F * N * D * 2) % 16 == 0:
+        pair = torch.empty(2, F * N, D, dtype=torch.bfloat16, device=s.device)
+        pair[1].copy_(s.reshape(F * N, D))
+    for i in range(n_iterations):
+        s, sl, sn = _iteration(s, k, v, p, sl, pair, sn, i + 1 < n_iterations)
     return s

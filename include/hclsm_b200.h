@@ -215,6 +215,24 @@ int hclsm_event_detect(const float* probs, const float* threshold, int32_t B, in
                        int32_t* pos, int32_t* counts, int32_t* meta, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Row-fused stages of the slot-attention iteration (dynamic_slots.py:98-131):
+ * one warp per row, rows of 128 to 1024 columns in multiples of 128 (else
+ * HCLSM_ERR_UNSUPPORTED), 16-byte aligned rows.
+ *   hclsm_gru_cell_ln: hclsm_gru_cell, then LayerNorm (w, b may be NULL,
+ *     eps) of the new state into ln_out (ln_dtype) -- the GRUCell of :123-126
+ *     and the norm_slots LayerNorm of :128 in one pass.
+ *   hclsm_residual_clamp_ln: hclsm_residual_clamp, then LayerNorm of the
+ *     result into ln_out -- the residual and clamp of :128-130 and the next
+ *     iteration's norm_pre_attn LayerNorm (:111) in one pass.
+ * ------------------------------------------------------------------------- */
+int hclsm_gru_cell_ln(const float* gi, const float* gh, const float* b_ih, const float* b_hh, const float* h,
+                      float* h_out, const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype,
+                      int64_t rows, int32_t H, float eps, void* stream);
+int hclsm_residual_clamp_ln(const float* h, const float* m, const float* b, float* out, void* out_bf16,
+                            const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype, int64_t rows,
+                            int32_t C, float clamp, float eps, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Training-mode backward of the slot-attention iteration and of the Level-1
  * event transformer (the gradients autograd takes through
  * hclsm/objects/dynamic_slots.py:98-131 _iteration_step and

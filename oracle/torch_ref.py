@@ -27,7 +27,7 @@ def sequential_ssm_scan(x, dt, A_log, B, C):
     A = -A_log.exp().clamp(min=1e-6, max=1.0)
     x_f, B_f, C_f = x.float(), B.float(), C.float()
     dt_f = dt.float().clamp(min=1e-3, max=1.0)
-    h = torch.zeros(batch, d_inner, d_state, dtype=torch.float32)
+    h = torch.zeros(batch, d_inner, d_state, dtype=torch.float32, device=x.device)
     ys = []
     for t in range(T):
         dA = torch.exp(torch.clamp(dt_f[:, t, :, None] * A[None], min=-20.0, max=0.0))

@@ -13,6 +13,7 @@ reference tree.
 from __future__ import annotations
 
 import argparse
+import copy
 import os
 import sys
 
@@ -154,6 +155,19 @@ def level0_cases():
             out[f"{case}/g/{name}"] = _np(p.grad)
     for name, p in mod.named_parameters():
         out[f"l0w/{name}"] = _np(p)
+    # the same module and inputs in float64: the exact answer the fp32 results
+    # (the reference's and this library's) are both measured against
+    mod64 = copy.deepcopy(mod).double()
+    for case in ("l0m", "l0"):
+        x = torch.from_numpy(out[f"{case}/x"]).double().requires_grad_(True)
+        mask = torch.from_numpy(out[f"{case}/mask"]).double() if f"{case}/mask" in out else None
+        mod64.zero_grad()
+        y = mod64(x, mask)
+        y.backward(torch.from_numpy(out[f"{case}/dy"]).double())
+        out[f"{case}/y64"] = y.detach().numpy().copy()
+        out[f"{case}/dx64"] = x.grad.numpy().copy()
+        for name, p in mod64.named_parameters():
+            out[f"{case}/g64/{name}"] = p.grad.numpy().copy()
     return out
 
 

@@ -1,7 +1,7 @@
 """Level0SSM around its blocks: the masked mean over objects and the
 nan_to_num / clamp / mask epilogue kernels against torch's own ops, and the
 patched Level0SSM.forward against the reference's golden vectors (fp32:
-1e-4 relative; rel = max|err| / max|ref|)."""
+1e-5 relative to the exact answer; rel = max|err| / max|ref|)."""
 import os
 
 import numpy as np
@@ -82,6 +82,15 @@ class _Level0(nn.Module):
 
 @pytest.mark.parametrize("case", ["l0m", "l0"])
 def test_patched_level0_matches_reference_golden(case):
+    """Forward and every gradient against the exact answer (the reference
+    module run in float64 by the fixture generator), and against the
+    reference's own fp32 result within 1e-5 plus that result's distance from
+    the exact answer.  Against the exact answer the bar is 1e-5, except 2e-5
+    in the masked case: there the gradient of the first global block's A_log
+    (a sum over the two videos' ten steps of products that carry the masked
+    mean of inputs reaching 400) is ill-conditioned in fp32 -- the reference's
+    fp32 result on the CPU is 9.9e-6 from exact, the same formula in plain
+    PyTorch fp32 on the GPU 1.23e-5, this library 1.61e-5."""
     g = np.load(GOLD)
     mod = _Level0().cuda()
     with torch.no_grad():
@@ -90,8 +99,11 @@ def test_patched_level0_matches_reference_golden(case):
     x = torch.from_numpy(g[f"{case}/x"]).cuda().requires_grad_(True)
     m = torch.from_numpy(g[f"{case}/mask"]).cuda() if f"{case}/mask" in g.files else None
     y = level0_forward(mod, x, m)
-    assert rel_err(y.detach().cpu().numpy(), g[f"{case}/y"]) < 1e-4
     y.backward(torch.from_numpy(g[f"{case}/dy"]).cuda())
-    assert rel_err(x.grad.cpu().numpy(), g[f"{case}/dx"]) < 1e-4
-    for name, p in mod.named_parameters():
-        assert rel_err(p.grad.cpu().numpy(), g[f"{case}/g/{name}"]) < 1e-4, name
+    pairs = [("y", y.detach(), g[f"{case}/y"], g[f"{case}/y64"]),
+             ("dx", x.grad, g[f"{case}/dx"], g[f"{case}/dx64"])]
+    pairs += [(name, p.grad, g[f"{case}/g/{name}"], g[f"{case}/g64/{name}"]) for name, p in mod.named_parameters()]
+    for name, got, ref32, ref64 in pairs:
+        got = got.cpu().numpy()
+        assert rel_err(got, ref64) < (2e-5 if case == "l0m" else 1e-5), (name, rel_err(got, ref64))
+        assert rel_err(got, ref32) < 1e-5 + rel_err(ref32, ref64), name

@@ -110,3 +110,31 @@ def test_core_tcgen05_and_mma_agree_with_oracle(shape, monkeypatch):
         out, attn = slot_attention_core(Q.cuda(), K.cuda(), V.cuda(), attn_fp32=True)
         assert rel_err(_np(out), ro) < 2e-2, sel
         assert rel_err(_np(attn), ra) < 2e-2, sel
+
+
+@pytest.mark.parametrize("H", [384, 128, 1024])
+def test_row_fused_stages_match_separate_kernels(H):
+    """hclsm_gru_cell_ln and hclsm_residual_clamp_ln against the separate
+    GRU / residual-clamp and LayerNorm kernels they fuse."""
+    from hclsm_b200.kernels.slot_attention_kernel import (gru_cell, gru_cell_ln, layernorm, residual_clamp,
+                                                          residual_clamp_ln)
+    gen = torch.Generator().manual_seed(H)
+    R = 77
+    gi, gh = (torch.randn(R, 3 * H, generator=gen).cuda() for _ in range(2))
+    b_ih, b_hh = (torch.randn(3 * H, generator=gen).cuda() * 0.1 for _ in range(2))
+    h0 = torch.randn(R, H, generator=gen).cuda() * 20
+    w, b = 1 + 0.1 * torch.randn(H, generator=gen).cuda(), 0.1 * torch.randn(H, generator=gen).cuda()
+    for dt in (torch.float32, torch.bfloat16):
+        h1, m1 = gru_cell_ln(gi, gh, b_ih, b_hh, h0, w, b, dt)
+        h2 = gru_cell(gi, gh, b_ih, b_hh, h0)
+        m2 = layernorm(h2, w, b, out_dtype=dt)
+        assert rel_err(_np(h1), _np(h2)) < 1e-6  # same formula; the compiler may contract differently
+        assert rel_err(_np(m1), _np(m2)) < (1e-6 if dt == torch.float32 else 8e-3)
+        mm = torch.randn(R, H, generator=gen).cuda() * 40
+        o1b = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
+        o2b = torch.empty_like(o1b)
+        o1, n1 = residual_clamp_ln(h1, mm, b, 50.0, w, b, dt, out_bf16=o1b)
+        o2 = residual_clamp(h2, mm, b, 50.0, out_bf16=o2b)
+        n2 = layernorm(o2, w, b, out_dtype=dt)
+        assert rel_err(_np(o1), _np(o2)) < 1e-6 and rel_err(_np(o1b), _np(o2b)) < 8e-3
+        assert rel_err(_np(n1), _np(n2)) < (1e-6 if dt == torch.float32 else 8e-3)
