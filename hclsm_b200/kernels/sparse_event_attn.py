@@ -23,7 +23,7 @@ from dataclasses import dataclass, field
 import torch
 
 from .. import _lib
-from .slot_attention_kernel import layernorm, residual_clamp
+from .slot_attention_kernel import layernorm, residual_clamp, residual_clamp_ln
 
 __all__ = ["sparse_event_attn_fn", "EventTransformer", "event_compact", "event_detect", "event_gather", "event_scatter",
            "sparse_event_attention_fused"]
@@ -247,22 +247,36 @@ class EventTransformer:
         if key_padding_mask is not None:
             kp = _c(key_padding_mask.to(torch.uint8))
         lib = _lib.load()
-        for ly in self.layers:
-            h = layernorm(x, ly.ln1_w, ly.ln1_b, out_dtype=dt)
+        # each residual add and the LayerNorm after it run as one row kernel
+        # where the row fits (E a multiple of 128, at most 1024)
+        fuse = E % 128 == 0 and E <= 1024
+        nl = len(self.layers)
+        h = layernorm(x, self.layers[0].ln1_w, self.layers[0].ln1_b, out_dtype=dt) if nl else None
+        for i, ly in enumerate(self.layers):
             qkv = _c(torch.mm(h, ly.w_qkv_t))
             a = torch.empty(R, E, dtype=dt, device=x.device)
             rc = lib.hclsm_event_mha(_lib.ptr(qkv), _lib.ptr(kp), _lib.ptr(a), n, N, H, hd, float(hd ** -0.5),
                                      _lib.dtype_code(dt), _lib.stream_ptr(x.device))
             _lib.check(rc, "hclsm_event_mha")
-            x = residual_clamp(x, self._mm(a, ly.w_o_t), None, 0.0)
-            h = layernorm(x, ly.ln2_w, ly.ln2_b, out_dtype=dt)
+            if fuse:
+                x, h = residual_clamp_ln(x, self._mm(a, ly.w_o_t), None, 0.0, ly.ln2_w, ly.ln2_b, dt)
+            else:
+                x = residual_clamp(x, self._mm(a, ly.w_o_t), None, 0.0)
+                h = layernorm(x, ly.ln2_w, ly.ln2_b, out_dtype=dt)
             u = self._mm(h, ly.w13_t)
             F = u.shape[1] // 2
             s = torch.empty(R, F, dtype=dt, device=x.device)
             rc = lib.hclsm_swiglu(_lib.ptr(u), _lib.ptr(s), R, F, _lib.dtype_code(dt), _lib.stream_ptr(x.device))
             _lib.check(rc, "hclsm_swiglu")
-            x = residual_clamp(x, self._mm(s, ly.w2_t), None, 0.0)
-        h = layernorm(x, self.norm_w, self.norm_b, out_dtype=dt)
+            nw, nb = ((self.layers[i + 1].ln1_w, self.layers[i + 1].ln1_b) if i + 1 < nl
+                      else (self.norm_w, self.norm_b))
+            if fuse:
+                x, h = residual_clamp_ln(x, self._mm(s, ly.w2_t), None, 0.0, nw, nb, dt)
+            else:
+                x = residual_clamp(x, self._mm(s, ly.w2_t), None, 0.0)
+                h = layernorm(x, nw, nb, out_dtype=dt)
+        if not nl:
+            h = layernorm(x, self.norm_w, self.norm_b, out_dtype=dt)
         y = self._mm(h, self.w_out_t)
         return y.reshape(n, N, -1).to(frames.dtype)
 
