@@ -540,7 +540,7 @@ def run_config0(args, rank, world, dev, peaks, flush):
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks[0]["hbm_gbs"], "unit": "GB/s",
                         "frac": gbs / peaks[0]["hbm_gbs"], "peak_source": peaks[1],
                         "note": "4.3 MB per call: launch-latency bound (0.7 us at HBM speed)"}}
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         t = cpu_scan(32, 16, 512, 16, bwd=False, dtype_name="float32", gated=True)
         leg["cpu_baseline"] = {"value": t * 1e3, "unit": "ms", "cores": _cpu_threads(), "kind": "port",
                                "sample": "the whole config-0 call: sequential_ssm_scan restated in PyTorch on "
@@ -580,7 +580,7 @@ def run_config1(args, rank, world, dev, peaks, flush):
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks[0]["hbm_gbs"], "unit": "GB/s",
                         "frac": gbs / peaks[0]["hbm_gbs"], "peak_source": peaks[1],
                         "note": "whole step (fwd + bwd kernels + autograd glue); the kernels are SFU/issue bound"}}
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         n = 32
         t = cpu_scan(n, 64, 768, 16, bwd=True, dtype_name="bfloat16", reps=2)
         leg["cpu_baseline"] = {"value": n / t, "unit": "sequences/s", "cores": _cpu_threads(), "kind": "port",
@@ -654,12 +654,72 @@ def run_slot(args, rank, world, dev, peaks, flush):
             leg["verify"] = {"rel_err_vs_single_gpu": float((got - ref).abs().max() / ref.abs().max()),
                              "tol": 2e-2}
             leg["verify"]["verified"] = leg["verify"]["rel_err_vs_single_gpu"] < 2e-2
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         t = cpu_slot()
         leg["cpu_baseline"] = {"value": 128 / t, "unit": "frames/s", "cores": _cpu_threads(), "kind": "port",
                                "sample": "the whole config-2 step (k/v projections + 3 x _iteration_step restated "
                                          "in PyTorch, fp32) on the host, best of 3"}
     del g
+    return leg
+
+
+def run_slot_train(args, rank, world, dev, peaks, flush):
+    """Config 2 in training mode: 3 differentiable _iteration_steps (this
+    library's forward and backward kernels, bf16 weight products with fp32
+    accumulation) on 128 frames, forward + backward of sum(slots * w) into the
+    slots, k, v and every iteration parameter; k and v are given."""
+    import torch
+
+    from hclsm_b200.kernels.training import slot_iteration_train
+    from hclsm_b200.workloads import SlotIterModule, slot_inputs
+
+    d = slot_inputs(seed=11, device=dev)
+    W = d["weights"]
+    mod = SlotIterModule.from_weights(W, 384, dev)
+    k = torch.nn.functional.linear(d["inputs"], W["project_k.weight"]).to(torch.bfloat16)
+    v = torch.nn.functional.linear(d["inputs"], W["project_v.weight"]).to(torch.bfloat16)
+    w = torch.randn(d["slots"].shape, device=dev)
+    leaves = [t.detach().clone().requires_grad_(True) for t in (d["slots"], k, v)]
+
+    def step():
+        for t in leaves + list(mod.parameters()):
+            t.grad = None
+        s = leaves[0]
+        for _ in range(3):
+            s = slot_iteration_train(mod, s, leaves[1], leaves[2], torch.bfloat16)
+        (s * w).sum().backward()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    ms = _timed(step, 10, dev, flush)
+    (ms,) = _max_over_ranks([ms], dev, world)
+    leg = {"metric": "slot_attention_train_frames_per_s", "value": 128 / (ms * 1e-3), "unit": "frames/s",
+           "ms_per_step": ms,
+           "config": "BASELINE config 2 shapes in training mode: 3 x _iteration_step forward + backward "
+                     "(autograd through this library's kernels), 128 frames x 32 slots x 196 tokens x 384, bf16 "
+                     "weight products; per rank; L2 flushed between steps"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import torch_ref
+
+        torch.set_num_threads(_cpu_threads())
+        dc = slot_inputs(seed=11)
+        Wc = {n: t.clone().requires_grad_(True) for n, t in dc["weights"].items()}
+        kc = torch.nn.functional.linear(dc["inputs"], dc["weights"]["project_k.weight"])
+        vc = torch.nn.functional.linear(dc["inputs"], dc["weights"]["project_v.weight"])
+        wc = torch.randn(dc["slots"].shape)
+
+        def cpu_step():
+            lv = [t.detach().clone().requires_grad_(True) for t in (dc["slots"], kc, vc)]
+            s = lv[0]
+            for _ in range(3):
+                s = torch_ref.iteration_step(s, lv[1], lv[2], Wc)
+            (s * wc).sum().backward()
+
+        t = _best_of(cpu_step, reps=2)
+        leg["cpu_baseline"] = {"value": 128 / t, "unit": "frames/s", "cores": _cpu_threads(), "kind": "port",
+                               "sample": "the whole step on the host: 3 x _iteration_step restated in PyTorch, "
+                                         "fp32, forward + autograd backward, best of 2"}
     return leg
 
 
@@ -708,7 +768,7 @@ def run_event(args, rank, world, dev, peaks, flush):
             got = torch.cat(full, 0).float()
             r = float((got - ref.float()).abs().max() / ref.float().abs().max())
             leg["verify"] = {"rel_err_vs_single_gpu": r, "tol": 2e-2, "verified": r < 2e-2}
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         t, nev = cpu_event()
         leg["cpu_baseline"] = {"value": nev / t, "unit": "event frames/s", "cores": _cpu_threads(), "kind": "port",
                                "sample": "the whole config-3 call (naive_sparse_event_attention + the Level-1 "
@@ -800,9 +860,10 @@ def main():
         legs["config2_slot_attention"] = run_slot(args, rank, world, dev, peaks, flush)
         legs["config3_event_attention"] = run_event(args, rank, world, dev, peaks, flush)
         legs["ssm_block"] = run_ssm_block(args, rank, world, dev, flush)
+        legs["config2_slot_attention_train"] = run_slot_train(args, rank, world, dev, peaks, flush)
         del flush
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:
         n = args.ref_seqs
         sec = cpu_scan(n, L, DI, DS, bwd=True, dtype_name="bfloat16", reps=1, seed=1234)
         sec_c, thr_c = cpu_scan_c(16)

@@ -175,3 +175,30 @@ def ssm_block_inputs(nseq=256, T=64, d_model=384, d_state=16, seed=0, device="cp
     g = torch.Generator(device="cpu").manual_seed(seed + 1)
     x = torch.randn(nseq, T, d_model, generator=g).to(device)
     return blk, x
+
+
+class SlotIterModule(torch.nn.Module):
+    """The parameters DynamicSlotAttention._iteration_step uses
+    (hclsm/objects/dynamic_slots.py:52-83) under the same attribute names, so
+    hclsm_b200.kernels.training.slot_iteration_train runs on it without the
+    reference package."""
+
+    def __init__(self, d_slot: int):
+        super().__init__()
+        self.d_slot = d_slot
+        self.project_q = torch.nn.Linear(d_slot, d_slot, bias=False)
+        self.gru = torch.nn.GRUCell(d_slot, d_slot)
+        self.norm_slots = torch.nn.LayerNorm(d_slot)
+        self.mlp = torch.nn.Sequential(torch.nn.Linear(d_slot, 4 * d_slot), torch.nn.ReLU(),
+                                       torch.nn.Linear(4 * d_slot, d_slot))
+        self.norm_pre_attn = torch.nn.LayerNorm(d_slot)
+        self.scale = d_slot ** -0.5
+
+    @classmethod
+    def from_weights(cls, w: dict, d_slot: int, device="cpu"):
+        """Load the names of ``slot_inputs``' weight dict that this module has."""
+        mod = cls(d_slot).to(device)
+        with torch.no_grad():
+            for name, p in mod.named_parameters():
+                p.copy_(w[name])
+        return mod
