@@ -93,7 +93,11 @@ def _ssm_block_forward(self, x):
     B_param = self.B_proj(z)
     C_param = self.C_proj(z)
     y = ssm_scan(z, self.dt_proj(z), self.A_log, B_param, C_param, clamp=True, z=gate_pre, dt_softplus=True)
-    y = self.out_proj(y.to(residual.dtype))
+    # under autocast out_proj takes bf16 operands, which y already is: the
+    # reference's fp32 round trip (level0_ssm.py:101-105) would change no value
+    if not (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == y.dtype):
+        y = y.to(residual.dtype)
+    y = self.out_proj(y)
     return residual + y
 
 
