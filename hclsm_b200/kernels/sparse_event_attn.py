@@ -316,8 +316,13 @@ def sparse_event_attn_fn(states, event_mask, attn_fn, max_events=None, backend: 
     if backend not in ("auto", "b200", "optimized", "naive"):
         raise ValueError(f"unknown backend {backend!r}")
     _lib.require_cuda(states, event_mask)
-    if isinstance(attn_fn, EventTransformer) and max_events is None:
-        return sparse_event_attention_fused(states, event_mask, attn_fn)
+    grad = torch.is_grad_enabled()
+    if isinstance(attn_fn, EventTransformer):
+        if grad and states.requires_grad:
+            raise RuntimeError("hclsm_b200: an EventTransformer holds inference weights and has no backward; "
+                               "train through the Level1EventDynamics module (patched by install())")
+        if max_events is None:
+            return sparse_event_attention_fused(states, event_mask, attn_fn)
     states = _c(states)
     B, T, N, D = states.shape
     idx, pos, counts, meta = event_compact(event_mask)
@@ -329,6 +334,18 @@ def sparse_event_attn_fn(states, event_mask, attn_fn, max_events=None, backend: 
         rank = torch.cumsum(m.int(), dim=1) - 1
         m = m & (rank < max_events)
         idx, pos, counts, meta = event_compact(m.float())
+    if grad:
+        # differentiable gather / scatter: gradients reach the states through
+        # attn_fn at the events and directly everywhere else, as in the
+        # reference's clone-and-assign (:76-86)
+        from .training import event_gather_train, event_scatter_train
+
+        if states.requires_grad:
+            padded = event_gather_train(states, idx, pos, counts, meta, K)
+        else:
+            padded = event_gather(states, idx, counts, meta, B * K, pad_k=K)
+        upd = attn_fn(padded.reshape(B * K, N, D))
+        return event_scatter_train(states, upd.reshape(B, K, N, D), idx, pos, counts, meta, K)
     padded = event_gather(states, idx, counts, meta, B * K, pad_k=K)
     upd = attn_fn(padded.reshape(B * K, N, D))
     return event_scatter(states, upd.reshape(B * K, N, D).to(states.dtype), pos, counts, pad_k=K)

@@ -239,3 +239,37 @@ def test_event_mha_tcgen05_and_mma_vs_torch(frames, T, padded, monkeypatch):
         nan_ref = torch.isnan(ref)
         assert torch.equal(torch.isnan(o), nan_ref), sel
         assert rel_err(o[~nan_ref].cpu().numpy(), ref[~nan_ref].cpu().numpy()) < 2e-2, sel
+
+
+@pytest.mark.parametrize("max_events", [None, 2])
+def test_sparse_event_attn_fn_gradients(max_events):
+    """sparse_event_attn_fn with a Python attn_fn under autograd: gradients to
+    the states and to attn_fn's parameters equal those of the reference's
+    clone-and-assign loop (sparse_event_attn.py:35-86) restated in torch."""
+    from hclsm_b200.kernels import sparse_event_attn_fn
+    gen = torch.Generator().manual_seed(21)
+    B, T, N, D = 3, 9, 4, 16
+    states = torch.randn(B, T, N, D, generator=gen).cuda()
+    mask = (torch.rand(B, T, generator=gen) < 0.4).float().cuda()
+    mask[2] = 0.0
+    mask[2, 5] = 1.0
+    lin = torch.nn.Linear(D, D).cuda()
+    w = torch.randn(B, T, N, D, generator=gen).cuda()
+    s1 = states.clone().requires_grad_(True)
+    out = sparse_event_attn_fn(s1, mask, lambda f: torch.tanh(lin(f)), max_events=max_events)
+    (out * w).sum().backward()
+    g_lin = [p.grad.clone() for p in lin.parameters()]
+    lin.zero_grad()
+    s2 = states.clone().requires_grad_(True)
+    ref = s2.clone()
+    for b in range(B):
+        idx = torch.nonzero(mask[b] > 0.5).flatten()
+        if max_events is not None:
+            idx = idx[:max_events]
+        if len(idx):
+            ref[b, idx] = torch.tanh(lin(s2[b, idx]))
+    (ref * w).sum().backward()
+    assert rel_err(out.detach().cpu().numpy(), ref.detach().cpu().numpy()) < 1e-6
+    assert rel_err(s1.grad.cpu().numpy(), s2.grad.cpu().numpy()) < 1e-6
+    for a, p in zip(g_lin, lin.parameters()):
+        assert rel_err(a.cpu().numpy(), p.grad.cpu().numpy()) < 1e-5
