@@ -4,8 +4,8 @@ and for DynamicSlotAttention._iteration_step (hclsm/objects/dynamic_slots.py:98-
 * ``slot_attention_fn(Q, K, V, scale=None, backend="auto")`` keeps the reference
   signature (slot_attention_kernel.py:324-355) and returns ``(out, attn)`` with
   the softmax over the SLOT axis.  The forward runs the fused sm_100a core;
-  the backward applies the reference's own formulas (:215-236) with PyTorch
-  CUDA ops.  ``eps`` (keyword) adds to the softmax denominator: 0 for the
+  the backward applies the reference's own formulas (:215-236) with this
+  library's softmax-over-slots backward kernel and batched library GEMMs.  ``eps`` (keyword) adds to the softmax denominator: 0 for the
   naive/compiled reference paths, 1e-8 for its Triton path (:126).
 * ``slot_attention_iteration(slots, k, v, params)`` runs one full refinement
   step — LayerNorm, W_q, the attention core with the +-30 logit clamp, GRUCell,
@@ -64,23 +64,29 @@ class _SlotAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, Q, K, V, scale, eps):
         out, attn = slot_attention_core(Q, K, V, scale, eps=eps, attn_fp32=True)
-        ctx.save_for_backward(Q, K, V, attn)
-        ctx.scale = scale
+        ctx.save_for_backward(Q, K, V)
+        ctx.scale, ctx.eps = scale, eps
         return out.to(Q.dtype), attn if Q.dtype == torch.float32 else attn.to(Q.dtype)
 
     @staticmethod
     def backward(ctx, grad_out, grad_attn):
-        # the reference's backward (slot_attention_kernel.py:215-236)
-        Q, K, V, attn = ctx.saved_tensors
+        # the reference's backward (slot_attention_kernel.py:215-236): the
+        # probabilities are recomputed from Q K^T and the softmax-over-slots
+        # backward runs in this library's kernel; the contractions are batched
+        # library GEMMs in fp32
+        from .training import slot_softmax_bwd
+
+        Q, K, V = ctx.saved_tensors
         f = torch.float32
+        Qf, Kf, Vf = Q.to(f), K.to(f), V.to(f)
         go = grad_out.to(f)
-        d_attn = torch.bmm(go, V.to(f).transpose(1, 2))
+        d_attn = torch.bmm(go, Vf.transpose(1, 2))
         if grad_attn is not None:
             d_attn = d_attn + grad_attn.to(f)
-        sum_da = (attn * d_attn).sum(dim=1, keepdim=True)
-        d_logits = attn * (d_attn - sum_da) * ctx.scale
-        dQ = torch.bmm(d_logits, K.to(f)).to(Q.dtype)
-        dK = torch.bmm(d_logits.transpose(1, 2), Q.to(f)).to(K.dtype)
+        dots = torch.bmm(Qf, Kf.transpose(1, 2))
+        attn, d_dots = slot_softmax_bwd(dots, d_attn, ctx.scale, 0.0, ctx.eps, f)
+        dQ = torch.bmm(d_dots, Kf).to(Q.dtype)
+        dK = torch.bmm(d_dots.transpose(1, 2), Qf).to(K.dtype)
         dV = torch.bmm(attn.transpose(1, 2), go).to(V.dtype)
         return dQ, dK, dV, None, None
 
