@@ -386,6 +386,44 @@ def verify_config4(args, rank, world, dev, shard, y, grads, d):
     return out
 
 
+def run_weak(args, rank, world, dev):
+    """Secondary, N > 1 only: weak scaling -- every rank scans a full 8192-
+    sequence job of its own (its own seeded sequences), 2 timed steps; whole-
+    job rate = world x 8192 / max-over-ranks step time."""
+    import torch
+
+    from hclsm_b200.kernels.ssm_scan_kernel import bwd_workspace_bytes, scan_bwd_raw, scan_fwd_raw, states_bytes
+    from hclsm_b200.workloads import scan_inputs_range
+
+    n = GLOBAL_SEQS
+    d = scan_inputs_range(0, n, L, DI, DS, dtype=torch.bfloat16, seed=SEED + 1 + rank, device=dev)
+    ws = torch.empty(bwd_workspace_bytes(n, L, DI, DS), dtype=torch.uint8, device=dev)
+    st = torch.empty(states_bytes(n, L, DI, DS, torch.bfloat16), dtype=torch.uint8, device=dev)
+    y = torch.empty_like(d["x"])
+
+    def step():
+        scan_fwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], out=y, states=st)
+        return scan_bwd_raw(d["x"], d["dt"], d["A_log"], d["B"], d["C"], d["dy"], workspace=ws, states=st)
+
+    g = step()
+    del g
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(2):
+        g = step()
+        del g
+    e1.record()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    (ms,) = _max_over_ranks([e0.elapsed_time(e1) / 2], dev, world)
+    del d, ws, st, y
+    torch.cuda.empty_cache()
+    return {"value": world * n / (ms * 1e-3), "unit": "sequences/s", "ms_per_step": ms, "sequences_per_gpu": n,
+            "note": "secondary: weak scaling, each rank a full 8192-sequence job"}
+
+
 def run_e2e(args, rank, world, dev):
     """The public API end to end: inputs in pinned host memory; per step the
     H2D copy, ssm_scan_fn forward + autograd backward, and the D2H copy of y
@@ -851,6 +889,7 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     peaks = _peaks()
     r = run_config4(args, rank, world, dev)
+    weak = run_weak(args, rank, world, dev) if world > 1 and not args.no_extra else None
     e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)
     legs = {}
     if not args.no_extra:
@@ -894,7 +933,7 @@ def main():
                 "roofline_fwd": {"kernel": "scan_fwd_bf16x2_kernel (hclsm_ssm_scan_fwd_states)", "achieved": bw_fwd,
                                  "frac": bw_fwd / hbm, "ms": r["fwd_ms"], "algorithmic_bytes": fwd_bytes,
                                  "exp_floor_ms": nloc * L * DI * DS / (16 * 148 * 1.965e9) * 1e3},
-                "verify": r.get("verify"), "cpu_baseline": cpu, "e2e": e2e, "clocks": r["clocks"],
+                "verify": r.get("verify"), "weak_scaling": weak, "cpu_baseline": cpu, "e2e": e2e, "clocks": r["clocks"],
                 "legs": legs, "gpu_launches": 5 * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -56,6 +56,8 @@ SIGNATURES = {
     "hclsm_event_scatter": (ctypes.c_int, [_vp] * 5 + [_i64, _i64, _i32, _i32, _i32, _vp]),
     "hclsm_event_mha": (ctypes.c_int, [_vp] * 3 + [_i32] * 4 + [ctypes.c_float, _i32, _vp]),
     "hclsm_swiglu": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _vp]),
+    "hclsm_slot_attn_iter_workspace_size": (_sz, [_i32] * 3),
+    "hclsm_slot_attn_iter": (ctypes.c_int, [_vp] * 6 + [_i32] * 4 + [_vp, _sz, _vp]),
     "hclsm_gru_cell_ln": (ctypes.c_int, [_vp] * 9 + [_i32, _i64, _i32, ctypes.c_float, _vp]),
     "hclsm_residual_clamp_ln": (ctypes.c_int, [_vp] * 8 + [_i32, _i64, _i32, ctypes.c_float, ctypes.c_float, _vp]),
     "hclsm_colsum_workspace_size": (_sz, [_i32]),
@@ -71,6 +73,12 @@ SIGNATURES = {
     "hclsm_ssm_scan_bwd_noalloc_max_scratch": (_sz, []),
     "hclsm_ssm_scan_bwd_noalloc": (ctypes.c_int, [_vp] * 15 + [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
 }
+
+class SlotIterWeights(ctypes.Structure):
+    """hclsm_slot_iter_weights (include/hclsm_b200.h)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("wq_t", "w_ih_t", "w_hh_t", "b_ih", "b_hh", "w1_t", "b1", "w2_t", "b2",
+                                                "ln_attn_w", "ln_attn_b", "ln_mlp_w", "ln_mlp_b")]
+
 
 _lib = None
 

@@ -15,13 +15,14 @@ and for DynamicSlotAttention._iteration_step (hclsm/objects/dynamic_slots.py:98-
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
 from .. import _lib
 
-__all__ = ["slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration",
+__all__ = ["slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration", "slot_attn_iter",
            "layernorm", "gru_cell", "bias_act", "residual_clamp"]
 
 
@@ -304,3 +305,26 @@ def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations:
     for i in range(n_iterations):
         s, sl, sn = _iteration(s, k, v, p, sl, pair, sn, i + 1 < n_iterations)
     return s
+
+
+def slot_attn_iter(slots, k, v, p: SlotIterationParams, out_bf16=None):
+    """One _iteration_step through the single C entry point
+    hclsm_slot_attn_iter (bf16 weight products).  slots (F, N, D) fp32, k and
+    v (F, M, D) bf16.  Returns the new slots (fp32); their bf16 copy goes to
+    ``out_bf16`` when given."""
+    if p.dtype != torch.bfloat16:
+        raise TypeError("hclsm_slot_attn_iter runs bf16 weight products (SlotIterationParams dtype bfloat16)")
+    _lib.require_cuda(slots, k, v)
+    s = _c(slots.float())
+    k, v = _c(k.to(torch.bfloat16)), _c(v.to(torch.bfloat16))
+    F, N, D = s.shape
+    M = k.shape[1]
+    lib = _lib.load()
+    ws = torch.empty(max(lib.hclsm_slot_attn_iter_workspace_size(F, N, D), 1), dtype=torch.uint8, device=s.device)
+    w = _lib.SlotIterWeights(*[_lib.ptr(t) for t in (p.wq_t, p.w_ih_t, p.w_hh_t, p.b_ih, p.b_hh, p.w1_t, p.b1_bf16,
+                                                      p.w2_t, p.b2, p.ln_attn_w, p.ln_attn_b, p.ln_mlp_w, p.ln_mlp_b)])
+    out = torch.empty_like(s)
+    rc = lib.hclsm_slot_attn_iter(_lib.ptr(s), _lib.ptr(k), _lib.ptr(v), ctypes.byref(w), _lib.ptr(out),
+                                  _lib.ptr(out_bf16), F, N, M, D, _lib.ptr(ws), ws.numel(), _lib.stream_ptr(s.device))
+    _lib.check(rc, "hclsm_slot_attn_iter")
+    return out

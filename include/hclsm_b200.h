@@ -215,6 +215,40 @@ int hclsm_event_detect(const float* probs, const float* threshold, int32_t B, in
                        int32_t* pos, int32_t* counts, int32_t* meta, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * One whole slot-attention refinement step: DynamicSlotAttention._iteration_step
+ * (hclsm/objects/dynamic_slots.py:98-131), the slot-attention entry point of
+ * the reference's hot path as one call.  bf16 weight products (fp32
+ * accumulation, library GEMMs), fp32 carried state:
+ *   slots (F, N, D) f32 -> slots_out (F, N, D) f32 (+ an optional bf16 copy);
+ *   k, v (F, M, D) bf16 (the module's k / v projections of its inputs).
+ * Weights are transposed for x @ W^T ((in, out) row-major, bf16); biases and
+ * LayerNorm affines f32 (b1 bf16: it is the epilogue bias of the MLP's first
+ * product; affines and b2 may be NULL).  Workspace:
+ * hclsm_slot_attn_iter_workspace_size(F, N, D) bytes, 256-byte aligned.
+ * D % 8 == 0; the attention core's limits apply (N <= 64, D <= 512).
+ * ------------------------------------------------------------------------- */
+typedef struct hclsm_slot_iter_weights {
+  const void* wq_t;          /* (D, D) bf16: project_q.weight^T */
+  const void* w_ih_t;        /* (D, 3D) bf16: gru.weight_ih^T */
+  const void* w_hh_t;        /* (D, 3D) bf16: gru.weight_hh^T */
+  const float* b_ih;         /* (3D) */
+  const float* b_hh;         /* (3D) */
+  const void* w1_t;          /* (D, 4D) bf16: mlp.0.weight^T */
+  const void* b1;            /* (4D) bf16: mlp.0.bias */
+  const void* w2_t;          /* (4D, D) bf16: mlp.2.weight^T */
+  const float* b2;           /* (D): mlp.2.bias */
+  const float* ln_attn_w;    /* norm_pre_attn */
+  const float* ln_attn_b;
+  const float* ln_mlp_w;     /* norm_slots */
+  const float* ln_mlp_b;
+} hclsm_slot_iter_weights;
+
+size_t hclsm_slot_attn_iter_workspace_size(int32_t F, int32_t N, int32_t D);
+int hclsm_slot_attn_iter(const float* slots, const void* k, const void* v, const hclsm_slot_iter_weights* w,
+                         float* slots_out, void* slots_out_bf16, int32_t F, int32_t N, int32_t M, int32_t D,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Row-fused stages of the slot-attention iteration (dynamic_slots.py:98-131):
  * one warp per row, rows of 128 to 1024 columns in multiples of 128 (else
  * HCLSM_ERR_UNSUPPORTED), 16-byte aligned rows.

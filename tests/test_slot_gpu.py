@@ -138,3 +138,28 @@ def test_row_fused_stages_match_separate_kernels(H):
         n2 = layernorm(o2, w, b, out_dtype=dt)
         assert rel_err(_np(o1), _np(o2)) < 1e-6 and rel_err(_np(o1b), _np(o2b)) < 8e-3
         assert rel_err(_np(n1), _np(n2)) < (1e-6 if dt == torch.float32 else 8e-3)
+
+
+@pytest.mark.parametrize("F,N,M,D", [(128, 32, 196, 384), (5, 20, 70, 128), (3, 8, 49, 64)])
+def test_slot_attn_iter_entry_point(F, N, M, D):
+    """hclsm_slot_attn_iter (the whole step behind one C call) against the
+    Python path's bf16 step and the oracle's fp32 step, three iterations."""
+    from hclsm_b200.kernels.slot_attention_kernel import slot_attn_iter
+    d = slot_inputs(F=F, N=N, M=M, D=D, seed=F + D)
+    W = d["weights"]
+    Wq = {k: t.to(torch.bfloat16).float() if t.dim() == 2 else t for k, t in W.items()}
+    inp = d["inputs"].to(torch.bfloat16).float()
+    k = (inp @ Wq["project_k.weight"].T).to(torch.bfloat16)
+    v = (inp @ Wq["project_v.weight"].T).to(torch.bfloat16)
+    p = SlotIterationParams.from_state(W, "cuda")
+    s1 = d["slots"].cuda()
+    s2 = d["slots"].cuda()
+    for _ in range(3):
+        s1 = slot_attn_iter(s1, k.cuda(), v.cuda(), p)
+        s2 = slot_attention_iterations(s2, k.cuda(), v.cuda(), p, 1)
+    assert rel_err(_np(s1), _np(s2)) < 2e-3
+    Wn = {kk: t.numpy() for kk, t in Wq.items()}
+    s = d["slots"].numpy()
+    for _ in range(3):
+        s = osl.iteration_step(s, k.float().numpy(), v.float().numpy(), Wn)
+    assert rel_err(_np(s1), s) < 2e-2
