@@ -23,6 +23,7 @@ import torch
 from .. import _lib
 
 __all__ = ["slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration", "slot_attn_iter",
+           "fold_query_into_keys",
            "layernorm", "gru_cell", "bias_act", "residual_clamp"]
 
 
@@ -235,7 +236,21 @@ def slot_attention_iteration(slots, k, v, p: SlotIterationParams, slots_lp=None,
     return out, out_lp
 
 
-def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_next_sn):
+def fold_query_into_keys(project_k_weight, project_q_weight, dtype=torch.bfloat16):
+    """The key projection with W_q folded in: (d_input, d_slot) = W_k^T W_q.
+
+    project_q and project_k have no bias (dynamic_slots.py:51-53), so the
+    attention logits of _iteration_step (:113-117) are
+    LN(s) W_q^T (x W_k^T)^T = LN(s) (x W_k^T W_q)^T: keys projected with this
+    weight (k' = x @ it, once per forward) let every refinement step feed the
+    normalised slots to the attention core directly, without its own W_q
+    product.  The product is formed in fp32 and rounded to ``dtype`` once."""
+    wk = project_k_weight.detach().float()
+    wq = project_q_weight.detach().float()
+    return (wk.t() @ wq).to(dtype).contiguous()
+
+
+def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_next_sn, keys_folded=False):
     """The step with its row stages fused: LayerNorm (skipped when ``sn``, the
     normalised slots, is given), W_q, the attention core, the GRU gate
     products, GRUCell + norm_slots LayerNorm (one kernel), the MLP, and
@@ -257,7 +272,10 @@ def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_nex
         slots_lp = s2.to(torch.bfloat16)
     if sn is None:
         sn = layernorm(s2, p.ln_attn_w, p.ln_attn_b, out_dtype=dt)
-    q = torch.mm(sn.reshape(R, D), p.wq_t).reshape(F, N, D)
+    if keys_folded:  # k holds x W_k^T W_q: the logits need LN(s) only
+        q = sn.reshape(F, N, D)
+    else:
+        q = torch.mm(sn.reshape(R, D), p.wq_t).reshape(F, N, D)
     if lp and pair is not None and p.w_gru_t is not None:
         slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False, out=pair[0].view(F, N, D))
         g2 = torch.bmm(pair, p.w_gru_t, out_dtype=torch.float32)
@@ -293,7 +311,10 @@ def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_nex
     return out.reshape(F, N, D), (out_lp.reshape(F, N, D) if lp else None), sn_next
 
 
-def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations: int):
+def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations: int, keys_folded: bool = False):
+    """``n_iterations`` refinement steps.  With ``keys_folded`` the keys are
+    x @ fold_query_into_keys(W_k, W_q) instead of x W_k^T and no step runs the
+    W_q product."""
     s = slots.float().contiguous()
     k = _c(k.to(p.dtype))
     v = _c(v.to(p.dtype))
@@ -303,7 +324,7 @@ def slot_attention_iterations(slots, k, v, p: SlotIterationParams, n_iterations:
         pair = torch.empty(2, F * N, D, dtype=torch.bfloat16, device=s.device)
         pair[1].copy_(s.reshape(F * N, D))
     for i in range(n_iterations):
-        s, sl, sn = _iteration(s, k, v, p, sl, pair, sn, i + 1 < n_iterations)
+        s, sl, sn = _iteration(s, k, v, p, sl, pair, sn, i + 1 < n_iterations, keys_folded)
     return s
 
 

@@ -9,7 +9,7 @@ import torch
 
 from conftest import rel_err
 from oracle import slot_attn as osl
-from hclsm_b200.kernels import (SlotIterationParams, slot_attention_core, slot_attention_fn,
+from hclsm_b200.kernels import (SlotIterationParams, fold_query_into_keys, slot_attention_core, slot_attention_fn,
                                 slot_attention_iterations)
 from hclsm_b200.workloads import slot_inputs
 
@@ -91,6 +91,28 @@ def test_config2_three_iterations_vs_oracle():
     for _ in range(3):
         s = osl.iteration_step(s, k.float().numpy(), v.float().numpy(), Wn)
     assert rel_err(_np(out), s) < 2e-2
+
+
+def test_config2_folded_keys_vs_oracle():
+    """Keys projected with W_k^T W_q (no per-step W_q product) against the
+    oracle's unfolded steps at 2e-2, and against this library's unfolded path."""
+    d = slot_inputs(seed=0)
+    W = d["weights"]
+    Wq = {k: t.to(torch.bfloat16).float() if t.dim() == 2 else t for k, t in W.items()}
+    inp = d["inputs"].to(torch.bfloat16)
+    k = (inp.float() @ Wq["project_k.weight"].T).to(torch.bfloat16)
+    v = (inp.float() @ Wq["project_v.weight"].T).to(torch.bfloat16)
+    p = SlotIterationParams.from_state(W, "cuda")
+    wkq = fold_query_into_keys(W["project_k.weight"], W["project_q.weight"]).cuda()
+    kf = torch.mm(inp.cuda().reshape(-1, inp.shape[-1]), wkq).reshape(k.shape)
+    out = slot_attention_iterations(d["slots"].cuda(), kf, v.cuda(), p, 3, keys_folded=True)
+    plain = slot_attention_iterations(d["slots"].cuda(), k.cuda(), v.cuda(), p, 3)
+    Wn = {kk: t.numpy() for kk, t in Wq.items()}
+    s = d["slots"].numpy()
+    for _ in range(3):
+        s = osl.iteration_step(s, k.float().numpy(), v.float().numpy(), Wn)
+    assert rel_err(_np(out), s) < 2e-2
+    assert rel_err(_np(out), _np(plain)) < 2e-2
 
 
 @pytest.mark.parametrize("shape", [(128, 32, 196, 384), (3, 5, 33, 128), (2, 64, 130, 256)])
