@@ -23,6 +23,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+// four gate values as fp32 from fp32 or bf16 storage (16- or 8-byte load)
+__device__ __forceinline__ float4 ldg4(const float* p) { return ld4(p); }
+__device__ __forceinline__ float4 ldg4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
 __device__ __forceinline__ float at(const float4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
 
 // LayerNorm of a row held as NV float4 per lane (lane l owns columns
@@ -67,10 +75,11 @@ __device__ __forceinline__ void row_layernorm(const float4 (&v)[NV], int lane, c
 }
 
 // torch.nn.GRUCell (gates r, z, n; gi = x W_ih^T, gh = h W_hh^T without
-// biases, fp32; the arithmetic of hclsm_gru_cell), then LayerNorm of the new
-// state.  One warp per row of H = 128 NV columns.
-template <int NV, typename TO>
-__global__ void gru_ln_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
+// biases, stored as TG = fp32 or bf16; gate arithmetic in fp32 as in
+// hclsm_gru_cell), then LayerNorm of the new state.  One warp per row of
+// H = 128 NV columns.
+template <int NV, typename TO, typename TG>
+__global__ void gru_ln_kernel(const TG* __restrict__ gi, const TG* __restrict__ gh,
                               const float* __restrict__ b_ih, const float* __restrict__ b_hh,
                               const float* __restrict__ h, float* __restrict__ h_out, const float* __restrict__ lnw,
                               const float* __restrict__ lnb, TO* __restrict__ ln_out, int64_t rows, float eps) {
@@ -80,14 +89,14 @@ __global__ void gru_ln_kernel(const float* __restrict__ gi, const float* __restr
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
-  const float* gir = gi + r * 3 * H;
-  const float* ghr = gh + r * 3 * H;
+  const TG* gir = gi + r * 3 * H;
+  const TG* ghr = gh + r * 3 * H;
   float4 v[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int c = 4 * lane + 128 * j;
-    const float4 ir = ld4(gir + c), iz = ld4(gir + H + c), in = ld4(gir + 2 * H + c);
-    const float4 hr = ld4(ghr + c), hz = ld4(ghr + H + c), hn = ld4(ghr + 2 * H + c);
+    const float4 ir = ldg4(gir + c), iz = ldg4(gir + H + c), in = ldg4(gir + 2 * H + c);
+    const float4 hr = ldg4(ghr + c), hz = ldg4(ghr + H + c), hn = ldg4(ghr + 2 * H + c);
     const float4 bir = ld4(b_ih + c), biz = ld4(b_ih + H + c), bin = ld4(b_ih + 2 * H + c);
     const float4 bhr = ld4(b_hh + c), bhz = ld4(b_hh + H + c), bhn = ld4(b_hh + 2 * H + c);
     const float4 hv = ld4(h + r * H + c);
@@ -153,14 +162,14 @@ __global__ void residual_clamp_ln_kernel(const float* __restrict__ h, const floa
 using namespace hclsm;
 using namespace hclsm::slotfused;
 
-template <typename TO>
-static int launch_gru_ln(int nv, unsigned blocks, cudaStream_t st, const float* gi, const float* gh, const float* b_ih,
+template <typename TO, typename TG>
+static int launch_gru_ln(int nv, unsigned blocks, cudaStream_t st, const TG* gi, const TG* gh, const float* b_ih,
                          const float* b_hh, const float* h, float* h_out, const float* w, const float* b, TO* y,
                          int64_t rows, float eps) {
   switch (nv) {
 #define HCLSM_GRU_LN(NV) \
   case NV:                \
-    return launch_pdl(gru_ln_kernel<NV, TO>, blocks, 256, 0, st, gi, gh, b_ih, b_hh, h, h_out, w, b, y, rows, eps);
+    return launch_pdl(gru_ln_kernel<NV, TO, TG>, blocks, 256, 0, st, gi, gh, b_ih, b_hh, h, h_out, w, b, y, rows, eps);
     HCLSM_GRU_LN(1) HCLSM_GRU_LN(2) HCLSM_GRU_LN(3) HCLSM_GRU_LN(4)
     HCLSM_GRU_LN(5) HCLSM_GRU_LN(6) HCLSM_GRU_LN(7) HCLSM_GRU_LN(8)
 #undef HCLSM_GRU_LN
@@ -185,9 +194,23 @@ static int launch_res_ln(int nv, unsigned blocks, cudaStream_t st, const float* 
 
 static bool al16(const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-extern "C" int hclsm_gru_cell_ln(const float* gi, const float* gh, const float* b_ih, const float* b_hh,
-                                 const float* h, float* h_out, const float* ln_w, const float* ln_b, void* ln_out,
-                                 int32_t ln_dtype, int64_t rows, int32_t H, float eps, void* stream) {
+template <typename TG>
+static int gru_ln_dispatch(int32_t ln_dtype, int nv, unsigned blocks, cudaStream_t st, const TG* gi, const TG* gh,
+                           const float* b_ih, const float* b_hh, const float* h, float* h_out, const float* ln_w,
+                           const float* ln_b, void* ln_out, int64_t rows, float eps) {
+  if (ln_dtype == HCLSM_BF16)
+    return launch_gru_ln(nv, blocks, st, gi, gh, b_ih, b_hh, h, h_out, ln_w, ln_b,
+                         static_cast<__nv_bfloat16*>(ln_out), rows, eps);
+  if (ln_dtype == HCLSM_F32)
+    return launch_gru_ln(nv, blocks, st, gi, gh, b_ih, b_hh, h, h_out, ln_w, ln_b, static_cast<float*>(ln_out), rows,
+                         eps);
+  return HCLSM_ERR_DTYPE;
+}
+
+extern "C" int hclsm_gru_cell_ln(const void* gi, const void* gh, int32_t gate_dtype, const float* b_ih,
+                                 const float* b_hh, const float* h, float* h_out, const float* ln_w,
+                                 const float* ln_b, void* ln_out, int32_t ln_dtype, int64_t rows, int32_t H,
+                                 float eps, void* stream) {
   if (!gi || !gh || !b_ih || !b_hh || !h || !h_out || !ln_out) return HCLSM_ERR_NULL;
   if (rows < 0 || H <= 0) return HCLSM_ERR_SHAPE;
   if (H % 128 != 0 || H > 1024) return HCLSM_ERR_UNSUPPORTED;
@@ -196,12 +219,13 @@ extern "C" int hclsm_gru_cell_ln(const float* gi, const float* gh, const float* 
   if (rows == 0) return HCLSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned blocks = (unsigned)((rows + 7) / 8);
-  if (ln_dtype == HCLSM_BF16)
-    return launch_gru_ln(H / 128, blocks, st, gi, gh, b_ih, b_hh, h, h_out, ln_w, ln_b,
-                         static_cast<__nv_bfloat16*>(ln_out), rows, eps);
-  if (ln_dtype == HCLSM_F32)
-    return launch_gru_ln(H / 128, blocks, st, gi, gh, b_ih, b_hh, h, h_out, ln_w, ln_b, static_cast<float*>(ln_out),
-                         rows, eps);
+  if (gate_dtype == HCLSM_F32)
+    return gru_ln_dispatch(ln_dtype, H / 128, blocks, st, static_cast<const float*>(gi),
+                           static_cast<const float*>(gh), b_ih, b_hh, h, h_out, ln_w, ln_b, ln_out, rows, eps);
+  if (gate_dtype == HCLSM_BF16)
+    return gru_ln_dispatch(ln_dtype, H / 128, blocks, st, static_cast<const __nv_bfloat16*>(gi),
+                           static_cast<const __nv_bfloat16*>(gh), b_ih, b_hh, h, h_out, ln_w, ln_b, ln_out, rows,
+                           eps);
   return HCLSM_ERR_DTYPE;
 }
 

@@ -23,9 +23,10 @@ extern "C" int hclsm_layernorm(const float* x, const float* w, const float* b, v
                                float eps, int32_t out_dtype, void* stream);
 extern "C" int hclsm_gru_cell(const float* gi, const float* gh, const float* b_ih, const float* b_hh,
                               const float* h, float* h_out, int64_t rows, int32_t H, void* stream);
-extern "C" int hclsm_gru_cell_ln(const float* gi, const float* gh, const float* b_ih, const float* b_hh,
-                                 const float* h, float* h_out, const float* ln_w, const float* ln_b, void* ln_out,
-                                 int32_t ln_dtype, int64_t rows, int32_t H, float eps, void* stream);
+extern "C" int hclsm_gru_cell_ln(const void* gi, const void* gh, int32_t gate_dtype, const float* b_ih,
+                                 const float* b_hh, const float* h, float* h_out, const float* ln_w,
+                                 const float* ln_b, void* ln_out, int32_t ln_dtype, int64_t rows, int32_t H,
+                                 float eps, void* stream);
 extern "C" int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* out, void* out_bf16,
                                     int64_t rows, int32_t C, float clamp, void* stream);
 
@@ -58,8 +59,8 @@ struct Layout {
     sn = take(2 * R * D);       // LN(slots), bf16
     q = take(2 * R * D);        // q, bf16
     upd = take(2 * R * D);      // attention updates, bf16
-    gi = take(4 * R * 3 * D);   // fp32
-    gh = take(4 * R * 3 * D);   // fp32
+    gi = take(4 * R * 3 * D);   // fp32 (bf16 on the row-fused path)
+    gh = take(4 * R * 3 * D);   // fp32 (bf16 on the row-fused path)
     h = take(4 * R * D);        // GRU state, fp32
     mln = take(2 * R * D);      // LN(h), bf16
     m1 = take(2 * R * 4 * D);   // relu(.. W1^T + b1), bf16
@@ -178,12 +179,15 @@ extern "C" int hclsm_slot_attn_iter(const float* slots, const void* k, const voi
   if ((rc = hclsm_slot_attn_core(q, k, v, upd, nullptr, F, N, M, D, (float)(1.0 / sqrt((double)D)), 30.0f, 0.0f, HCLSM_BF16,
                                  0, stream)))
     return rc;
-  if ((rc = gemm(lt, upd, w->w_ih_t, gi, CUDA_R_32F, R, 3 * D, D, nullptr, ltws, kLtWorkspace, st))) return rc;
-  if ((rc = gemm(lt, sb, w->w_hh_t, gh, CUDA_R_32F, R, 3 * D, D, nullptr, ltws, kLtWorkspace, st))) return rc;
+  // the row-fused GRU kernel reads bf16 gate products (what the reference's
+  // GRUCell receives under bf16 autocast); the separate one reads fp32
   const bool fused = D % 128 == 0 && D <= 1024;
+  const cudaDataType_t gt = fused ? CUDA_R_16BF : CUDA_R_32F;
+  if ((rc = gemm(lt, upd, w->w_ih_t, gi, gt, R, 3 * D, D, nullptr, ltws, kLtWorkspace, st))) return rc;
+  if ((rc = gemm(lt, sb, w->w_hh_t, gh, gt, R, 3 * D, D, nullptr, ltws, kLtWorkspace, st))) return rc;
   if (fused) {
-    rc = hclsm_gru_cell_ln(gi, gh, w->b_ih, w->b_hh, slots, h, w->ln_mlp_w, w->ln_mlp_b, mln, HCLSM_BF16, R, D, 1e-5f,
-                           stream);
+    rc = hclsm_gru_cell_ln(gi, gh, HCLSM_BF16, w->b_ih, w->b_hh, slots, h, w->ln_mlp_w, w->ln_mlp_b, mln, HCLSM_BF16,
+                           R, D, 1e-5f, stream);
   } else {
     rc = hclsm_gru_cell(gi, gh, w->b_ih, w->b_hh, slots, h, R, D, stream);
     if (!rc) rc = hclsm_layernorm(h, w->ln_mlp_w, w->ln_mlp_b, mln, R, D, 1e-5f, HCLSM_BF16, stream);

@@ -146,12 +146,15 @@ def residual_clamp(h, m, b, clamp=50.0, out=None, out_bf16=None):
 
 
 def gru_cell_ln(gi, gh, b_ih, b_hh, h, ln_w, ln_b, ln_dtype, eps=1e-5):
-    """(GRUCell state fp32, LayerNorm of it in ln_dtype) in one pass."""
+    """(GRUCell state fp32, LayerNorm of it in ln_dtype) in one pass; the gate
+    products gi and gh are fp32 or bf16 (both the same)."""
     H = h.shape[-1]
     rows = h.numel() // H
+    if gi.dtype != gh.dtype:
+        raise TypeError("hclsm_b200: gru_cell_ln wants gi and gh of one dtype")
     out = torch.empty_like(h)
     ln = torch.empty(h.shape, dtype=ln_dtype, device=h.device)
-    rc = _lib.load().hclsm_gru_cell_ln(_lib.ptr(gi), _lib.ptr(gh), _lib.ptr(b_ih), _lib.ptr(b_hh), _lib.ptr(h),
+    rc = _lib.load().hclsm_gru_cell_ln(_lib.ptr(gi), _lib.ptr(gh), _lib.dtype_code(gi.dtype), _lib.ptr(b_ih), _lib.ptr(b_hh), _lib.ptr(h),
                                        _lib.ptr(out), _lib.ptr(ln_w), _lib.ptr(ln_b), _lib.ptr(ln),
                                        _lib.dtype_code(ln_dtype), rows, H, float(eps), _lib.stream_ptr(h.device))
     _lib.check(rc, "hclsm_gru_cell_ln")
@@ -278,7 +281,9 @@ def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_nex
         q = torch.mm(sn.reshape(R, D), p.wq_t).reshape(F, N, D)
     if lp and pair is not None and p.w_gru_t is not None:
         slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False, out=pair[0].view(F, N, D))
-        g2 = torch.bmm(pair, p.w_gru_t, out_dtype=torch.float32)
+        # gate products rounded to bf16, as the reference's GRUCell receives
+        # them under bf16 autocast (gate arithmetic and state stay fp32)
+        g2 = torch.bmm(pair, p.w_gru_t)
         gi, gh = g2[0], g2[1]
     else:
         upd, _ = slot_attention_core(q, k, v, p.scale, clamp=30.0, eps=0.0, return_attn=False)
@@ -288,7 +293,7 @@ def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_nex
     if fuse:
         h, m = gru_cell_ln(gi, gh, p.b_ih, p.b_hh, s2, p.ln_mlp_w, p.ln_mlp_b, dt)
     else:
-        h = gru_cell(gi, gh, p.b_ih, p.b_hh, s2)
+        h = gru_cell(gi.float(), gh.float(), p.b_ih, p.b_hh, s2)
         m = layernorm(h, p.ln_mlp_w, p.ln_mlp_b, out_dtype=dt)
     if lp and p.b1_bf16 is not None:
         # bias + ReLU in the library GEMM's epilogue, bf16 out (the MLP runs in

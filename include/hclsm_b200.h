@@ -254,14 +254,17 @@ int hclsm_slot_attn_iter(const float* slots, const void* k, const void* v, const
  * HCLSM_ERR_UNSUPPORTED), 16-byte aligned rows.
  *   hclsm_gru_cell_ln: hclsm_gru_cell, then LayerNorm (w, b may be NULL,
  *     eps) of the new state into ln_out (ln_dtype) -- the GRUCell of :123-126
- *     and the norm_slots LayerNorm of :128 in one pass.
+ *     and the norm_slots LayerNorm of :128 in one pass.  The gate products gi
+ *     and gh are HCLSM_F32 or HCLSM_BF16 (gate_dtype; bf16 is what the
+ *     reference's GRUCell sees under bf16 autocast); the gate arithmetic and
+ *     the state are fp32.
  *   hclsm_residual_clamp_ln: hclsm_residual_clamp, then LayerNorm of the
  *     result into ln_out -- the residual and clamp of :128-130 and the next
  *     iteration's norm_pre_attn LayerNorm (:111) in one pass.
  * ------------------------------------------------------------------------- */
-int hclsm_gru_cell_ln(const float* gi, const float* gh, const float* b_ih, const float* b_hh, const float* h,
-                      float* h_out, const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype,
-                      int64_t rows, int32_t H, float eps, void* stream);
+int hclsm_gru_cell_ln(const void* gi, const void* gh, int32_t gate_dtype, const float* b_ih, const float* b_hh,
+                      const float* h, float* h_out, const float* ln_w, const float* ln_b, void* ln_out,
+                      int32_t ln_dtype, int64_t rows, int32_t H, float eps, void* stream);
 int hclsm_residual_clamp_ln(const float* h, const float* m, const float* b, float* out, void* out_bf16,
                             const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype, int64_t rows,
                             int32_t C, float clamp, float eps, void* stream);

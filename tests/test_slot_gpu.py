@@ -160,6 +160,12 @@ def test_row_fused_stages_match_separate_kernels(H):
         n2 = layernorm(o2, w, b, out_dtype=dt)
         assert rel_err(_np(o1), _np(o2)) < 1e-6 and rel_err(_np(o1b), _np(o2b)) < 8e-3
         assert rel_err(_np(n1), _np(n2)) < (1e-6 if dt == torch.float32 else 8e-3)
+    # bf16 gate products: the same as the fp32 kernel on the rounded values
+    gib, ghb = gi.to(torch.bfloat16), gh.to(torch.bfloat16)
+    h3, m3 = gru_cell_ln(gib, ghb, b_ih, b_hh, h0, w, b, torch.float32)
+    h4 = gru_cell(gib.float(), ghb.float(), b_ih, b_hh, h0)
+    assert rel_err(_np(h3), _np(h4)) < 1e-6
+    assert rel_err(_np(m3), _np(layernorm(h4, w, b, out_dtype=torch.float32))) < 1e-6
 
 
 @pytest.mark.parametrize("F,N,M,D", [(128, 32, 196, 384), (5, 20, 70, 128), (3, 8, 49, 64)])
