@@ -59,7 +59,8 @@ SIGNATURES = {
     "hclsm_slot_attn_iter_workspace_size": (_sz, [_i32] * 3),
     "hclsm_slot_attn_iter": (ctypes.c_int, [_vp] * 6 + [_i32] * 4 + [_vp, _sz, _vp]),
     "hclsm_gru_cell_ln": (ctypes.c_int, [_vp, _vp, _i32] + [_vp] * 7 + [_i32, _i64, _i32, ctypes.c_float, _vp]),
-    "hclsm_residual_clamp_ln": (ctypes.c_int, [_vp] * 8 + [_i32, _i64, _i32, ctypes.c_float, ctypes.c_float, _vp]),
+    "hclsm_residual_clamp_ln": (ctypes.c_int, [_vp, _vp, _i32] + [_vp] * 6 + [_i32, _i64, _i32, ctypes.c_float,
+                                                                           ctypes.c_float, _vp]),
     "hclsm_colsum_workspace_size": (_sz, [_i32]),
     "hclsm_colsum": (ctypes.c_int, [_vp, _vp, _i64, _i32, _vp, _sz, _vp]),
     "hclsm_layernorm_bwd_workspace_size": (_sz, [_i64, _i32]),

@@ -115,10 +115,10 @@ __global__ void gru_ln_kernel(const TG* __restrict__ gi, const TG* __restrict__ 
   row_layernorm<NV, TO>(v, lane, lnw, lnb, eps, ln_out + r * H);
 }
 
-// s = clamp((h + m) + b, -c, c) (fp32, plus an optional bf16 copy), then
-// LayerNorm of s.
-template <int NV, typename TO>
-__global__ void residual_clamp_ln_kernel(const float* __restrict__ h, const float* __restrict__ m,
+// s = clamp((h + m) + b, -c, c) (fp32, plus an optional bf16 copy; m stored
+// as TM = fp32 or bf16), then LayerNorm of s.
+template <int NV, typename TO, typename TM>
+__global__ void residual_clamp_ln_kernel(const float* __restrict__ h, const TM* __restrict__ m,
                                          const float* __restrict__ b, float* __restrict__ out,
                                          __nv_bfloat16* __restrict__ out_bf16, const float* __restrict__ lnw,
                                          const float* __restrict__ lnb, TO* __restrict__ ln_out, int64_t rows, float c,
@@ -133,7 +133,7 @@ __global__ void residual_clamp_ln_kernel(const float* __restrict__ h, const floa
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int col = 4 * lane + 128 * j;
-    const float4 hv = ld4(h + r * C + col), mv = ld4(m + r * C + col);
+    const float4 hv = ld4(h + r * C + col), mv = ldg4(m + r * C + col);
     float s[4] = {hv.x + mv.x, hv.y + mv.y, hv.z + mv.z, hv.w + mv.w};
     if (b) {
       const float4 bb = ld4(b + col);
@@ -177,14 +177,14 @@ static int launch_gru_ln(int nv, unsigned blocks, cudaStream_t st, const TG* gi,
   return HCLSM_ERR_UNSUPPORTED;
 }
 
-template <typename TO>
-static int launch_res_ln(int nv, unsigned blocks, cudaStream_t st, const float* h, const float* m, const float* bias,
+template <typename TO, typename TM>
+static int launch_res_ln(int nv, unsigned blocks, cudaStream_t st, const float* h, const TM* m, const float* bias,
                          float* out, __nv_bfloat16* ob, const float* w, const float* b, TO* y, int64_t rows, float c,
                          float eps) {
   switch (nv) {
 #define HCLSM_RES_LN(NV) \
   case NV:                \
-    return launch_pdl(residual_clamp_ln_kernel<NV, TO>, blocks, 256, 0, st, h, m, bias, out, ob, w, b, y, rows, c, eps);
+    return launch_pdl(residual_clamp_ln_kernel<NV, TO, TM>, blocks, 256, 0, st, h, m, bias, out, ob, w, b, y, rows, c, eps);
     HCLSM_RES_LN(1) HCLSM_RES_LN(2) HCLSM_RES_LN(3) HCLSM_RES_LN(4)
     HCLSM_RES_LN(5) HCLSM_RES_LN(6) HCLSM_RES_LN(7) HCLSM_RES_LN(8)
 #undef HCLSM_RES_LN
@@ -229,9 +229,22 @@ extern "C" int hclsm_gru_cell_ln(const void* gi, const void* gh, int32_t gate_dt
   return HCLSM_ERR_DTYPE;
 }
 
-extern "C" int hclsm_residual_clamp_ln(const float* h, const float* m, const float* b, float* out, void* out_bf16,
-                                       const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype,
-                                       int64_t rows, int32_t C, float clamp, float eps, void* stream) {
+template <typename TM>
+static int res_ln_dispatch(int32_t ln_dtype, int nv, unsigned blocks, cudaStream_t st, const float* h, const TM* m,
+                           const float* b, float* out, __nv_bfloat16* ob, const float* ln_w, const float* ln_b,
+                           void* ln_out, int64_t rows, float clamp, float eps) {
+  if (ln_dtype == HCLSM_BF16)
+    return launch_res_ln(nv, blocks, st, h, m, b, out, ob, ln_w, ln_b, static_cast<__nv_bfloat16*>(ln_out), rows,
+                         clamp, eps);
+  if (ln_dtype == HCLSM_F32)
+    return launch_res_ln(nv, blocks, st, h, m, b, out, ob, ln_w, ln_b, static_cast<float*>(ln_out), rows, clamp, eps);
+  return HCLSM_ERR_DTYPE;
+}
+
+extern "C" int hclsm_residual_clamp_ln(const float* h, const void* m, int32_t m_dtype, const float* b, float* out,
+                                       void* out_bf16, const float* ln_w, const float* ln_b, void* ln_out,
+                                       int32_t ln_dtype, int64_t rows, int32_t C, float clamp, float eps,
+                                       void* stream) {
   if (!h || !m || !out || !ln_out) return HCLSM_ERR_NULL;
   if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
   if (C % 128 != 0 || C > 1024) return HCLSM_ERR_UNSUPPORTED;
@@ -240,11 +253,11 @@ extern "C" int hclsm_residual_clamp_ln(const float* h, const float* m, const flo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   auto* ob = static_cast<__nv_bfloat16*>(out_bf16);
-  if (ln_dtype == HCLSM_BF16)
-    return launch_res_ln(C / 128, blocks, st, h, m, b, out, ob, ln_w, ln_b, static_cast<__nv_bfloat16*>(ln_out), rows,
-                         clamp, eps);
-  if (ln_dtype == HCLSM_F32)
-    return launch_res_ln(C / 128, blocks, st, h, m, b, out, ob, ln_w, ln_b, static_cast<float*>(ln_out), rows, clamp,
-                         eps);
+  if (m_dtype == HCLSM_F32)
+    return res_ln_dispatch(ln_dtype, C / 128, blocks, st, h, static_cast<const float*>(m), b, out, ob, ln_w, ln_b,
+                           ln_out, rows, clamp, eps);
+  if (m_dtype == HCLSM_BF16)
+    return res_ln_dispatch(ln_dtype, C / 128, blocks, st, h, static_cast<const __nv_bfloat16*>(m), b, out, ob, ln_w,
+                           ln_b, ln_out, rows, clamp, eps);
   return HCLSM_ERR_DTYPE;
 }

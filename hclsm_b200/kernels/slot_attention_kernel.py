@@ -162,12 +162,12 @@ def gru_cell_ln(gi, gh, b_ih, b_hh, h, ln_w, ln_b, ln_dtype, eps=1e-5):
 
 
 def residual_clamp_ln(h, m, b, clamp, ln_w, ln_b, ln_dtype, out_bf16=None, eps=1e-5):
-    """(clamp(h + m + b) fp32, LayerNorm of it in ln_dtype) in one pass; the
-    optional bf16 copy of the first goes to out_bf16."""
+    """(clamp(h + m + b) fp32, LayerNorm of it in ln_dtype) in one pass; m is
+    fp32 or bf16; the optional bf16 copy of the first goes to out_bf16."""
     C = h.shape[-1]
     out = torch.empty_like(h)
     ln = torch.empty(h.shape, dtype=ln_dtype, device=h.device)
-    rc = _lib.load().hclsm_residual_clamp_ln(_lib.ptr(h), _lib.ptr(m), _lib.ptr(b), _lib.ptr(out), _lib.ptr(out_bf16),
+    rc = _lib.load().hclsm_residual_clamp_ln(_lib.ptr(h), _lib.ptr(m), _lib.dtype_code(m.dtype), _lib.ptr(b), _lib.ptr(out), _lib.ptr(out_bf16),
                                              _lib.ptr(ln_w), _lib.ptr(ln_b), _lib.ptr(ln), _lib.dtype_code(ln_dtype),
                                              h.numel() // C, C, float(clamp), float(eps), _lib.stream_ptr(h.device))
     _lib.check(rc, "hclsm_residual_clamp_ln")
@@ -303,13 +303,16 @@ def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_nex
         m = torch._addmm_activation(p.b1, m, p.w1_t)  # fp32 throughout
     else:
         m = bias_act(_mm(m, p.w1_t), p.b1, "relu", torch.bfloat16)
-    m = _mm(m, p.w2_t)
+    sn_fused = want_next_sn and fuse
+    # the MLP output in bf16 where the fused residual kernel reads it (the
+    # reference's MLP output under autocast); fp32 otherwise
+    m = torch.mm(m, p.w2_t) if (lp and sn_fused) else _mm(m, p.w2_t)
     if lp:
         out_lp = pair[1] if pair is not None else torch.empty(R, D, dtype=torch.bfloat16, device=slots.device)
     else:
         out_lp = None
     sn_next = None
-    if want_next_sn and fuse:
+    if sn_fused:
         out, sn_next = residual_clamp_ln(h, m, p.b2, 50.0, p.ln_attn_w, p.ln_attn_b, dt, out_bf16=out_lp)
     else:
         out = residual_clamp(h, m, p.b2, 50.0, out_bf16=out_lp)

@@ -186,6 +186,12 @@ class EventTransformer:
             return torch.mm(a, w_t)
         return torch.mm(a, w_t, out_dtype=torch.float32)
 
+    def _mm_res(self, a, w_t):
+        """A product that the fused residual + LayerNorm kernel reads: in the
+        work dtype (bf16 under autocast, as the reference's Linear output),
+        the residual sum itself stays fp32."""
+        return torch.mm(a, w_t)
+
     def __call__(self, frames, key_padding_mask=None):
         """frames (n, N, d_slot) -> (n, N, d_slot); key_padding_mask (n, N) bool,
         True = dead slot (ignored as a key).  Replays a CUDA graph of the stack
@@ -259,7 +265,7 @@ class EventTransformer:
                                      _lib.dtype_code(dt), _lib.stream_ptr(x.device))
             _lib.check(rc, "hclsm_event_mha")
             if fuse:
-                x, h = residual_clamp_ln(x, self._mm(a, ly.w_o_t), None, 0.0, ly.ln2_w, ly.ln2_b, dt)
+                x, h = residual_clamp_ln(x, self._mm_res(a, ly.w_o_t), None, 0.0, ly.ln2_w, ly.ln2_b, dt)
             else:
                 x = residual_clamp(x, self._mm(a, ly.w_o_t), None, 0.0)
                 h = layernorm(x, ly.ln2_w, ly.ln2_b, out_dtype=dt)
@@ -271,7 +277,7 @@ class EventTransformer:
             nw, nb = ((self.layers[i + 1].ln1_w, self.layers[i + 1].ln1_b) if i + 1 < nl
                       else (self.norm_w, self.norm_b))
             if fuse:
-                x, h = residual_clamp_ln(x, self._mm(s, ly.w2_t), None, 0.0, nw, nb, dt)
+                x, h = residual_clamp_ln(x, self._mm_res(s, ly.w2_t), None, 0.0, nw, nb, dt)
             else:
                 x = residual_clamp(x, self._mm(s, ly.w2_t), None, 0.0)
                 h = layernorm(x, nw, nb, out_dtype=dt)

@@ -260,14 +260,15 @@ int hclsm_slot_attn_iter(const float* slots, const void* k, const void* v, const
  *     the state are fp32.
  *   hclsm_residual_clamp_ln: hclsm_residual_clamp, then LayerNorm of the
  *     result into ln_out -- the residual and clamp of :128-130 and the next
- *     iteration's norm_pre_attn LayerNorm (:111) in one pass.
+ *     iteration's norm_pre_attn LayerNorm (:111) in one pass.  m (the MLP
+ *     output) is HCLSM_F32 or HCLSM_BF16 (m_dtype); the sum is fp32.
  * ------------------------------------------------------------------------- */
 int hclsm_gru_cell_ln(const void* gi, const void* gh, int32_t gate_dtype, const float* b_ih, const float* b_hh,
                       const float* h, float* h_out, const float* ln_w, const float* ln_b, void* ln_out,
                       int32_t ln_dtype, int64_t rows, int32_t H, float eps, void* stream);
-int hclsm_residual_clamp_ln(const float* h, const float* m, const float* b, float* out, void* out_bf16,
-                            const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype, int64_t rows,
-                            int32_t C, float clamp, float eps, void* stream);
+int hclsm_residual_clamp_ln(const float* h, const void* m, int32_t m_dtype, const float* b, float* out,
+                            void* out_bf16, const float* ln_w, const float* ln_b, void* ln_out, int32_t ln_dtype,
+                            int64_t rows, int32_t C, float clamp, float eps, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Training-mode backward of the slot-attention iteration and of the Level-1

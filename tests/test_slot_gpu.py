@@ -166,6 +166,12 @@ def test_row_fused_stages_match_separate_kernels(H):
     h4 = gru_cell(gib.float(), ghb.float(), b_ih, b_hh, h0)
     assert rel_err(_np(h3), _np(h4)) < 1e-6
     assert rel_err(_np(m3), _np(layernorm(h4, w, b, out_dtype=torch.float32))) < 1e-6
+    # bf16 MLP output into the residual kernel: the same as fp32 on the rounded values
+    mmb = (torch.randn(R, H, generator=gen).cuda() * 40).to(torch.bfloat16)
+    o5, n5 = residual_clamp_ln(h3, mmb, b, 50.0, w, b, torch.float32)
+    o6 = residual_clamp(h3, mmb.float(), b, 50.0)
+    assert rel_err(_np(o5), _np(o6)) < 1e-6
+    assert rel_err(_np(n5), _np(layernorm(o6, w, b, out_dtype=torch.float32))) < 1e-6
 
 
 @pytest.mark.parametrize("F,N,M,D", [(128, 32, 196, 384), (5, 20, 70, 128), (3, 8, 49, 64)])
