@@ -636,7 +636,8 @@ def run_slot(args, rank, world, dev, peaks, flush):
     import torch
     import torch.distributed as dist
 
-    from hclsm_b200.kernels import SlotIterationParams, fold_query_into_keys, slot_attention_iterations
+    from hclsm_b200.kernels import (SlotIterationParams, key_value_weights, project_keys_values,
+                                    slot_attention_iterations)
     from hclsm_b200.shard import shard_range
     from hclsm_b200.workloads import slot_inputs
 
@@ -644,18 +645,14 @@ def run_slot(args, rank, world, dev, peaks, flush):
     W = d["weights"]
     p = SlotIterationParams.from_state(W, dev)
     # keys projected with W_k^T W_q (prepared once, like the transposed
-    # weights): the steps skip their W_q products
-    wk = fold_query_into_keys(W["project_k.weight"], W["project_q.weight"])
-    wv = W["project_v.weight"].to(torch.bfloat16).t().contiguous()
+    # weights): the steps skip their W_q products; k and v in one GEMM
+    w_kv = key_value_weights(W["project_k.weight"], W["project_v.weight"], W["project_q.weight"])
     f0, f1 = shard_range(128, rank, world)
     inp_all = d["inputs"].to(torch.bfloat16)
     slots_all = d["slots"]
 
     def run(inp, slots):
-        F_, M, D = inp.shape
-        x = inp.reshape(F_ * M, D)
-        k = torch.mm(x, wk).reshape(F_, M, D)
-        v = torch.mm(x, wv).reshape(F_, M, D)
+        k, v = project_keys_values(inp, w_kv)
         return slot_attention_iterations(slots, k, v, p, 3, keys_folded=True)
 
     inp, slots = inp_all[f0:f1].contiguous(), slots_all[f0:f1].contiguous()

@@ -3,6 +3,8 @@ from .ssm_scan_kernel import ssm_scan, ssm_scan_fn  # noqa: F401
 from .slot_attention_kernel import (  # noqa: F401
     SlotIterationParams,
     fold_query_into_keys,
+    key_value_weights,
+    project_keys_values,
     slot_attention_core,
     slot_attention_fn,
     slot_attention_iteration,
@@ -19,4 +21,5 @@ from .level0 import level0_epilogue, level0_forward, masked_mean_pool  # noqa: F
 
 __all__ = ["sparse_event_attn_fn", "EventTransformer", "sparse_event_attention_fused", "event_detect", "ssm_scan_fn",
            "ssm_scan", "slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration",
-           "slot_attention_iterations", "fold_query_into_keys", "masked_mean_pool", "level0_epilogue", "level0_forward"]
+           "slot_attention_iterations", "fold_query_into_keys", "key_value_weights", "project_keys_values",
+           "masked_mean_pool", "level0_epilogue", "level0_forward"]

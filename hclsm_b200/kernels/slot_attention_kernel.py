@@ -23,7 +23,7 @@ import torch
 from .. import _lib
 
 __all__ = ["slot_attention_fn", "slot_attention_core", "SlotIterationParams", "slot_attention_iteration", "slot_attn_iter",
-           "fold_query_into_keys",
+           "fold_query_into_keys", "key_value_weights", "project_keys_values",
            "layernorm", "gru_cell", "bias_act", "residual_clamp"]
 
 
@@ -251,6 +251,23 @@ def fold_query_into_keys(project_k_weight, project_q_weight, dtype=torch.bfloat1
     wk = project_k_weight.detach().float()
     wq = project_q_weight.detach().float()
     return (wk.t() @ wq).to(dtype).contiguous()
+
+
+def key_value_weights(project_k_weight, project_v_weight, project_q_weight=None, dtype=torch.bfloat16):
+    """(2, d_input, d_slot): [W_k^T (or W_k^T W_q, see fold_query_into_keys),
+    W_v^T] for project_keys_values."""
+    wk = (fold_query_into_keys(project_k_weight, project_q_weight, dtype) if project_q_weight is not None
+          else project_k_weight.detach().t().to(dtype))
+    return torch.stack([wk, project_v_weight.detach().t().to(dtype)]).contiguous()
+
+
+def project_keys_values(x, w_kv):
+    """k and v (dynamic_slots.py:152-154) of x (F, M, d_input) as one batched
+    library GEMM over the stacked weights (x is read through a stride-0 batch
+    view, not copied); both outputs contiguous (F, M, d_slot)."""
+    F, M, Din = x.shape
+    kv = torch.bmm(x.reshape(1, F * M, Din).expand(2, -1, -1), w_kv)
+    return kv[0].view(F, M, -1), kv[1].view(F, M, -1)
 
 
 def _iteration(slots, k, v, p: SlotIterationParams, slots_lp, pair, sn, want_next_sn, keys_folded=False):

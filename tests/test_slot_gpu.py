@@ -9,8 +9,8 @@ import torch
 
 from conftest import rel_err
 from oracle import slot_attn as osl
-from hclsm_b200.kernels import (SlotIterationParams, fold_query_into_keys, slot_attention_core, slot_attention_fn,
-                                slot_attention_iterations)
+from hclsm_b200.kernels import (SlotIterationParams, fold_query_into_keys, key_value_weights, project_keys_values,
+                                slot_attention_core, slot_attention_fn, slot_attention_iterations)
 from hclsm_b200.workloads import slot_inputs
 
 pytestmark = pytest.mark.gpu
@@ -105,6 +105,11 @@ def test_config2_folded_keys_vs_oracle():
     p = SlotIterationParams.from_state(W, "cuda")
     wkq = fold_query_into_keys(W["project_k.weight"], W["project_q.weight"]).cuda()
     kf = torch.mm(inp.cuda().reshape(-1, inp.shape[-1]), wkq).reshape(k.shape)
+    # the stacked k/v product gives the same keys and values
+    w_kv = key_value_weights(W["project_k.weight"], W["project_v.weight"], W["project_q.weight"]).cuda()
+    kf2, vf2 = project_keys_values(inp.cuda(), w_kv)
+    assert torch.equal(kf2, kf)
+    assert rel_err(_np(vf2), _np(v)) < 1e-2
     out = slot_attention_iterations(d["slots"].cuda(), kf, v.cuda(), p, 3, keys_folded=True)
     plain = slot_attention_iterations(d["slots"].cuda(), k.cuda(), v.cuda(), p, 3)
     Wn = {kk: t.numpy() for kk, t in Wq.items()}
