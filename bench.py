@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 0-3 legs")
+    ap.add_argument("--only", choices=["config0", "config1", "slot", "event", "block", "slot_train"],
+                    help="run this one leg alone (no config-4 step) and print its JSON line; for profiling")
     return ap.parse_args()
 
 
@@ -888,6 +890,20 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     peaks = _peaks()
+    if args.only:
+        flush = L2Flush(dev)
+        run = {"config0": lambda: run_config0(args, rank, world, dev, peaks, flush),
+               "config1": lambda: run_config1(args, rank, world, dev, peaks, flush),
+               "slot": lambda: run_slot(args, rank, world, dev, peaks, flush),
+               "event": lambda: run_event(args, rank, world, dev, peaks, flush),
+               "block": lambda: run_ssm_block(args, rank, world, dev, flush),
+               "slot_train": lambda: run_slot_train(args, rank, world, dev, peaks, flush)}[args.only]
+        leg = run()
+        if rank == 0:
+            print(json.dumps(dict(leg, n_gpus=world, leg=args.only)), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     r = run_config4(args, rank, world, dev)
     weak = run_weak(args, rank, world, dev) if world > 1 and not args.no_extra else None
     e2e = None if args.no_e2e else run_e2e(args, rank, world, dev)

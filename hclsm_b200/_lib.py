@@ -55,7 +55,7 @@ SIGNATURES = {
     "hclsm_event_gather": (ctypes.c_int, [_vp] * 5 + [_i64, _i32, _i32, _i64, _i32, _vp]),
     "hclsm_event_scatter": (ctypes.c_int, [_vp] * 5 + [_i64, _i64, _i32, _i32, _i32, _vp]),
     "hclsm_event_mha": (ctypes.c_int, [_vp] * 3 + [_i32] * 4 + [ctypes.c_float, _i32, _vp]),
-    "hclsm_swiglu": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _vp]),
+    "hclsm_swiglu": (ctypes.c_int, [_vp, _i32, _vp, _i64, _i32, _i32, _vp]),
     "hclsm_slot_attn_iter_workspace_size": (_sz, [_i32] * 3),
     "hclsm_slot_attn_iter": (ctypes.c_int, [_vp] * 6 + [_i32] * 4 + [_vp, _sz, _vp]),
     "hclsm_gru_cell_ln": (ctypes.c_int, [_vp, _vp, _i32] + [_vp] * 7 + [_i32, _i64, _i32, ctypes.c_float, _vp]),

@@ -390,17 +390,27 @@ __global__ void mha_f32_kernel(const float* __restrict__ qkv, const uint8_t* __r
   }
 }
 
-// SwiGLU: u (rows, 2C) fp32 holding [x W1^T | x W3^T] -> silu(a) * b.
-template <typename TO>
-__global__ void swiglu_kernel(const float* __restrict__ u, TO* __restrict__ y, int64_t rows, int C) {
+// SwiGLU: u (rows, 2C) holding [x W1^T | x W3^T] (TU = fp32 or bf16) ->
+// silu(a) * b in fp32, stored as TO.  A block walks rows, its threads walk
+// column pairs (one 8- or 4-byte load per half), no per-element division.
+template <typename TU, typename TO>
+__global__ void swiglu_kernel(const TU* __restrict__ u, TO* __restrict__ y, int64_t rows, int C) {
   pdl_wait();
   pdl_trigger();
-  const int64_t total = rows * C;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / C;
-    const int c = (int)(i % C);
-    const float a = u[r * 2 * C + c], bb = u[r * 2 * C + C + c];
-    io<TO>::st(y + i, a * sigmoid(a) * bb);
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const TU* ur = u + r * 2 * C;
+    TO* yr = y + r * C;
+    if ((C & 1) == 0) {
+      for (int c = 2 * threadIdx.x; c < C; c += 2 * blockDim.x) {
+        const float2 a = io<TU>::ld2(ur + c), g = io<TU>::ld2(ur + C + c);
+        io<TO>::st2(yr + c, a.x * sigmoid(a.x) * g.x, a.y * sigmoid(a.y) * g.y);
+      }
+    } else {
+      for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float a = io<TU>::ld(ur + c), g = io<TU>::ld(ur + C + c);
+        io<TO>::st(yr + c, a * sigmoid(a) * g);
+      }
+    }
   }
 }
 
@@ -544,17 +554,29 @@ extern "C" int hclsm_event_mha(const void* qkv, const uint8_t* key_pad, void* ou
   return HCLSM_ERR_UNSUPPORTED;
 }
 
-extern "C" int hclsm_swiglu(const float* u, void* y, int64_t rows, int32_t C, int32_t out_dtype, void* stream) {
+template <typename TU>
+static int swiglu_launch(const TU* u, void* y, int64_t rows, int32_t C, int32_t out_dtype, cudaStream_t st) {
+  const unsigned blocks = (unsigned)(rows < 148 * 16 ? rows : 148 * 16);
+  if (out_dtype == HCLSM_BF16)
+    return launch_pdl(swiglu_kernel<TU, __nv_bfloat16>, blocks, 256, 0, st, u, static_cast<__nv_bfloat16*>(y), rows,
+                      C);
+  if (out_dtype == HCLSM_F32)
+    return launch_pdl(swiglu_kernel<TU, float>, blocks, 256, 0, st, u, static_cast<float*>(y), rows, C);
+  return HCLSM_ERR_DTYPE;
+}
+
+extern "C" int hclsm_swiglu(const void* u, int32_t u_dtype, void* y, int64_t rows, int32_t C, int32_t out_dtype,
+                            void* stream) {
   if (!u || !y) return HCLSM_ERR_NULL;
   if (rows < 0 || C <= 0) return HCLSM_ERR_SHAPE;
   if (rows == 0) return HCLSM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (out_dtype == HCLSM_BF16)
-    return launch_pdl(swiglu_kernel<__nv_bfloat16>, ew_blocks(rows * C), 256, 0, st, u,
-                      static_cast<__nv_bfloat16*>(y), rows, C);
-  else if (out_dtype == HCLSM_F32)
-    return launch_pdl(swiglu_kernel<float>, ew_blocks(rows * C), 256, 0, st, u, static_cast<float*>(y), rows, C);
-  else
-    return HCLSM_ERR_DTYPE;
-  return cudaGetLastError() == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
+  // column pairs are read and written as one word: pointers aligned to a pair
+  const size_t us = u_dtype == HCLSM_BF16 ? 2 : 4, ys = out_dtype == HCLSM_BF16 ? 2 : 4;
+  if ((C & 1) == 0 &&
+      (reinterpret_cast<uintptr_t>(u) % (2 * us) != 0 || reinterpret_cast<uintptr_t>(y) % (2 * ys) != 0))
+    return HCLSM_ERR_ALIGN;
+  if (u_dtype == HCLSM_F32) return swiglu_launch(static_cast<const float*>(u), y, rows, C, out_dtype, st);
+  if (u_dtype == HCLSM_BF16) return swiglu_launch(static_cast<const __nv_bfloat16*>(u), y, rows, C, out_dtype, st);
+  return HCLSM_ERR_DTYPE;
 }

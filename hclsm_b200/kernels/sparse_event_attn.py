@@ -269,10 +269,11 @@ class EventTransformer:
             else:
                 x = residual_clamp(x, self._mm(a, ly.w_o_t), None, 0.0)
                 h = layernorm(x, ly.ln2_w, ly.ln2_b, out_dtype=dt)
-            u = self._mm(h, ly.w13_t)
+            u = self._mm_res(h, ly.w13_t)  # bf16 under autocast, as the reference's Linear output
             F = u.shape[1] // 2
             s = torch.empty(R, F, dtype=dt, device=x.device)
-            rc = lib.hclsm_swiglu(_lib.ptr(u), _lib.ptr(s), R, F, _lib.dtype_code(dt), _lib.stream_ptr(x.device))
+            rc = lib.hclsm_swiglu(_lib.ptr(u), _lib.dtype_code(u.dtype), _lib.ptr(s), R, F, _lib.dtype_code(dt),
+                                  _lib.stream_ptr(x.device))
             _lib.check(rc, "hclsm_swiglu")
             nw, nb = ((self.layers[i + 1].ln1_w, self.layers[i + 1].ln1_b) if i + 1 < nl
                       else (self.norm_w, self.norm_b))

@@ -257,7 +257,7 @@ class _Level1(torch.autograd.Function):
             u = _c(_mm(h2, torch.cat([w1, w3], 0).t(), dt))
             F_ = u.shape[1] // 2
             s = torch.empty(R, F_, dtype=dt, device=x.device)
-            _lib.check(lib.hclsm_swiglu(_lib.ptr(u), _lib.ptr(s), R, F_, _lib.dtype_code(dt),
+            _lib.check(lib.hclsm_swiglu(_lib.ptr(u), _lib.dtype_code(u.dtype), _lib.ptr(s), R, F_, _lib.dtype_code(dt),
                                         _lib.stream_ptr(x.device)), "hclsm_swiglu")
             saved += [x, h1, qkv, a, x1, h2, u, s]
             x = residual_clamp(x1, _c(_mm(s, w2.t(), dt)), None, 0.0)

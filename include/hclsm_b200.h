@@ -189,7 +189,8 @@ int hclsm_residual_clamp(const float* h, const float* m, const float* b, float* 
  *       nn.MultiheadAttention(bias=False) on a packed (frames*T, 3E) q|k|v
  *       matrix; key_pad (frames, T) bytes, non-zero = ignored key (NULL: none).
  *       bf16: T <= 64, head dim in {16, 32, 64, 128}, tensor cores.
- *   hclsm_swiglu: y = silu(u[:, :C]) * u[:, C:] (SwiGLUFFN, level1_event.py:28).
+ *   hclsm_swiglu: y = silu(u[:, :C]) * u[:, C:] (SwiGLUFFN, level1_event.py:28);
+ *     u fp32 or bf16 (u_dtype), arithmetic fp32.
  * frame_elems * element size must be a multiple of 16 bytes.
  * ------------------------------------------------------------------------- */
 int hclsm_event_compact(const void* mask, int32_t mask_dtype, int32_t B, int32_t T, int32_t* idx, int32_t* pos,
@@ -202,7 +203,7 @@ int hclsm_event_scatter(const void* states, const void* upd, const int32_t* pos,
                         void* stream);
 int hclsm_event_mha(const void* qkv, const uint8_t* key_pad, void* out, int32_t frames, int32_t T, int32_t H,
                     int32_t HD, float scale, int32_t dtype, void* stream);
-int hclsm_swiglu(const float* u, void* y, int64_t rows, int32_t C, int32_t out_dtype, void* stream);
+int hclsm_swiglu(const void* u, int32_t u_dtype, void* y, int64_t rows, int32_t C, int32_t out_dtype, void* stream);
 
 /* EventDetector's hard decision and the compaction in one launch
  * (hclsm/dynamics/event_detector.py:162-170 feeding hierarchy_manager.py:42-77):

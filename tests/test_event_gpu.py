@@ -273,3 +273,20 @@ def test_sparse_event_attn_fn_gradients(max_events):
     assert rel_err(s1.grad.cpu().numpy(), s2.grad.cpu().numpy()) < 1e-6
     for a, p in zip(g_lin, lin.parameters()):
         assert rel_err(a.cpu().numpy(), p.grad.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("C", [1536, 97])
+@pytest.mark.parametrize("udt", [torch.float32, torch.bfloat16])
+def test_swiglu_kernel(C, udt):
+    """hclsm_swiglu (SwiGLUFFN's silu(a) * b, level1_event.py:28) for fp32 and
+    bf16 products, even (column pairs) and odd C, against torch in fp32."""
+    from hclsm_b200 import _lib
+    gen = torch.Generator().manual_seed(C)
+    u = (torch.randn(301, 2 * C, generator=gen) * 3).to(udt).cuda()
+    ref = torch.nn.functional.silu(u[:, :C].float()) * u[:, C:].float()
+    for odt, tol in ((torch.float32, 1e-6), (torch.bfloat16, 8e-3)):
+        y = torch.empty(301, C, dtype=odt, device="cuda")
+        rc = _lib.load().hclsm_swiglu(_lib.ptr(u), _lib.dtype_code(udt), _lib.ptr(y), 301, C, _lib.dtype_code(odt),
+                                      _lib.stream_ptr(u.device))
+        _lib.check(rc, "hclsm_swiglu")
+        assert float((y.float() - ref).abs().max() / ref.abs().max()) < tol
