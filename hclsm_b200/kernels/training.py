@@ -127,6 +127,28 @@ def event_mha_bwd(qkv, key_pad, dout, frames, T, H, HD, scale):
     return dqkv
 
 
+def _lp(w, dt):
+    """w in the arithmetic dtype ``dt``.  For bf16 the cast of a parameter is
+    kept on the parameter and reused while its version counter is unchanged
+    (the three refinement steps and their backward passes of one training
+    step share one cast; an optimizer's in-place update bumps the version).
+    As for the inference caches, in-place changes that bypass the version
+    counter (``w.data`` edits) are not seen."""
+    if w.dtype == dt:
+        return w
+    if dt == F32:
+        return w.float()
+    ent = getattr(w, "_hclsm_lp", None)
+    if ent is not None and ent[0] == w._version and ent[1] == dt and ent[2] == w.data_ptr():
+        return ent[3]
+    cast = w.detach().to(dt)
+    try:
+        w._hclsm_lp = (w._version, dt, w.data_ptr(), cast)
+    except (AttributeError, RuntimeError):
+        pass
+    return cast
+
+
 def _mm(a, b, dt):
     """a @ b with fp32 output: fp32 operands for dt = fp32, bf16 operands
     (fp32 accumulation) for dt = bf16."""
@@ -150,15 +172,15 @@ class _SlotIteration(torch.autograd.Function):
         kd, vd = _c(k.to(dt)), _c(v.to(dt))
         b_ih32, b_hh32, b2_32 = b_ih.float().contiguous(), b_hh.float().contiguous(), b2.float().contiguous()
         sn = layernorm(s2, lna_w.float().contiguous(), lna_b.float().contiguous(), out_dtype=dt)
-        q = torch.mm(sn, wq.to(dt).t()).reshape(F_, N, D)
+        q = torch.mm(sn, _lp(wq, dt).t()).reshape(F_, N, D)
         upd, _ = slot_attention_core(q, kd, vd, scale, clamp=30.0, eps=0.0, return_attn=False)
         s_dt = s2 if dt == F32 else s2.to(dt)
-        gi = _c(_mm(upd.reshape(R, D), w_ih.t(), dt))
-        gh = _c(_mm(s_dt, w_hh.t(), dt))
+        gi = _c(_mm(upd.reshape(R, D), _lp(w_ih, dt).t(), dt))
+        gh = _c(_mm(s_dt, _lp(w_hh, dt).t(), dt))
         h = gru_cell(gi, gh, b_ih32, b_hh32, s2)
         mln = layernorm(h, lnm_w.float().contiguous(), lnm_b.float().contiguous(), out_dtype=dt)
-        m1 = torch._addmm_activation(b1.to(dt), mln, w1.to(dt).t())
-        m2 = _c(_mm(m1, w2.t(), dt))
+        m1 = torch._addmm_activation(b1.to(dt), mln, _lp(w1, dt).t())
+        m2 = _c(_mm(m1, _lp(w2, dt).t(), dt))
         out = residual_clamp(h, m2, b2_32, 50.0)
         ctx.save_for_backward(s2, kd, vd, sn, q, upd, gi, gh, h, mln, m1, m2, wq, w_ih, w_hh, b_ih32, b_hh32,
                               lna_w, lnm_w, w1, w2, b2_32)
@@ -177,10 +199,10 @@ class _SlotIteration(torch.autograd.Function):
         dpre = residual_clamp_bwd(h, m2, b2_32, dout.reshape(R, D), 50.0)
         db2 = colsum(dpre)
         dW2 = _wgrad(dpre, m1, dt)
-        dm1 = relu_bwd(m1, _mm(dpre, w2, dt), F32)
+        dm1 = relu_bwd(m1, _mm(dpre, _lp(w2, dt), dt), F32)
         db1 = colsum(dm1)
         dW1 = _wgrad(dm1, mln, dt)
-        dmln = _mm(dm1, w1, dt)
+        dmln = _mm(dm1, _lp(w1, dt), dt)
         dh, dlnm_w, dlnm_b = layernorm_bwd(h, lnm_w.float().contiguous(), dmln, dx=dpre.clone())
         # GRUCell
         d_gi, d_gh, ds = gru_cell_bwd(gi, gh, b_ih32, b_hh32, s2, dh)
@@ -188,8 +210,8 @@ class _SlotIteration(torch.autograd.Function):
         s_dt = s2 if dt == F32 else s2.to(dt)
         dW_ih = _wgrad(d_gi, upd.reshape(R, D), dt)
         dW_hh = _wgrad(d_gh, s_dt, dt)
-        d_upd = _mm(d_gi, w_ih, dt).reshape(F_, N, D)
-        ds += _mm(d_gh, w_hh, dt)
+        d_upd = _mm(d_gi, _lp(w_ih, dt), dt).reshape(F_, N, D)
+        ds += _mm(d_gh, _lp(w_hh, dt), dt)
         # attention core: softmax over slots of clamp(scale q k^T), weighted sum of v
         if dt == F32:
             d_attn = torch.bmm(d_upd, vd.transpose(1, 2))
@@ -209,7 +231,7 @@ class _SlotIteration(torch.autograd.Function):
             dk = torch.bmm(d_dots.transpose(1, 2), q, out_dtype=F32)
         dq = dq.reshape(R, D)
         dWq = _wgrad(dq, sn, dt)
-        dsn = _mm(dq, wq, dt)
+        dsn = _mm(dq, _lp(wq, dt), dt)
         ds, dlna_w, dlna_b = layernorm_bwd(s2, lna_w.float().contiguous(), dsn, dx=ds)
         sdt, kdt, vdt = ctx.in_dtypes
         return (ds.reshape(F_, N, D).to(sdt), dk.to(kdt), dv.to(vdt), dWq.to(wq.dtype), dW_ih.to(w_ih.dtype),
@@ -241,28 +263,28 @@ class _Level1(torch.autograd.Function):
         hd = E // H
         lib = _lib.load()
         fr = _c(frames.reshape(R, Ds))
-        x = _c(_mm(fr, w_in.t(), dt))
+        x = _c(_mm(fr, _lp(w_in, dt).t(), dt))
         saved = [fr]
         nl = len(layer_params) // _PER_LAYER
         for i in range(nl):
             n1w, n1b, wqkv, wo, n2w, n2b, w1, w3, w2 = layer_params[i * _PER_LAYER:(i + 1) * _PER_LAYER]
             h1 = layernorm(x, n1w.float().contiguous(), n1b.float().contiguous(), out_dtype=dt)
-            qkv = _c(torch.mm(h1, wqkv.to(dt).t()))
+            qkv = _c(torch.mm(h1, _lp(wqkv, dt).t()))
             a = torch.empty(R, E, dtype=dt, device=x.device)
             _lib.check(lib.hclsm_event_mha(_lib.ptr(qkv), _lib.ptr(key_pad), _lib.ptr(a), n, N, H, hd,
                                            float(hd ** -0.5), _lib.dtype_code(dt), _lib.stream_ptr(x.device)),
                        "hclsm_event_mha")
-            x1 = residual_clamp(x, _c(_mm(a, wo.t(), dt)), None, 0.0)
+            x1 = residual_clamp(x, _c(_mm(a, _lp(wo, dt).t(), dt)), None, 0.0)
             h2 = layernorm(x1, n2w.float().contiguous(), n2b.float().contiguous(), out_dtype=dt)
-            u = _c(_mm(h2, torch.cat([w1, w3], 0).t(), dt))
+            u = _c(_mm(h2, torch.cat([_lp(w1, dt), _lp(w3, dt)], 0).t(), dt))
             F_ = u.shape[1] // 2
             s = torch.empty(R, F_, dtype=dt, device=x.device)
             _lib.check(lib.hclsm_swiglu(_lib.ptr(u), _lib.dtype_code(u.dtype), _lib.ptr(s), R, F_, _lib.dtype_code(dt),
                                         _lib.stream_ptr(x.device)), "hclsm_swiglu")
             saved += [x, h1, qkv, a, x1, h2, u, s]
-            x = residual_clamp(x1, _c(_mm(s, w2.t(), dt)), None, 0.0)
+            x = residual_clamp(x1, _c(_mm(s, _lp(w2, dt).t(), dt)), None, 0.0)
         hf = layernorm(x, nw.float().contiguous(), nb.float().contiguous(), out_dtype=dt)
-        y = _mm(hf, w_out.t(), dt)
+        y = _mm(hf, _lp(w_out, dt).t(), dt)
         saved += [x, hf]
         ctx.save_for_backward(*saved, w_in, w_out, nw, *layer_params)
         ctx.meta = (n, N, Ds, E, H, hd, nl, dt, frames.dtype)
@@ -281,28 +303,28 @@ class _Level1(torch.autograd.Function):
         lp = sv[6 + 8 * nl:]
         dy = _c(dy.reshape(R, -1).float())
         g_out = _wgrad(dy, hf, dt)
-        dx, g_nw, g_nb = layernorm_bwd(xL, nw.float().contiguous(), _mm(dy, w_out, dt))
+        dx, g_nw, g_nb = layernorm_bwd(xL, nw.float().contiguous(), _mm(dy, _lp(w_out, dt), dt))
         grads = [None] * len(lp)
         for i in reversed(range(nl)):
             x, h1, qkv, a, x1, h2, u, s = per[8 * i:8 * i + 8]
             n1w, n1b, wqkv, wo, n2w, n2b, w1, w3, w2 = lp[i * _PER_LAYER:(i + 1) * _PER_LAYER]
             # x2 = x1 + w2(swiglu(w13 LN2(x1)))
             g_w2 = _wgrad(dx, s, dt)
-            du = swiglu_bwd(u, _mm(dx, w2, dt), F32)
+            du = swiglu_bwd(u, _mm(dx, _lp(w2, dt), dt), F32)
             g_w13 = _wgrad(du, h2, dt)
             Fh = du.shape[1] // 2
-            dx1, g_n2w, g_n2b = layernorm_bwd(x1, n2w.float().contiguous(), _mm(du, torch.cat([w1, w3], 0), dt),
+            dx1, g_n2w, g_n2b = layernorm_bwd(x1, n2w.float().contiguous(), _mm(du, torch.cat([_lp(w1, dt), _lp(w3, dt)], 0), dt),
                                               dx=dx.clone())
             # x1 = x + out_proj(mha(in_proj LN1(x)))
             g_wo = _wgrad(dx1, a, dt)
-            dqkv = event_mha_bwd(qkv, ctx.key_pad, _mm(dx1, wo, dt), n, N, H, hd, hd ** -0.5)
+            dqkv = event_mha_bwd(qkv, ctx.key_pad, _mm(dx1, _lp(wo, dt), dt), n, N, H, hd, hd ** -0.5)
             g_wqkv = _wgrad(dqkv, h1, dt)
-            dx, g_n1w, g_n1b = layernorm_bwd(x, n1w.float().contiguous(), _mm(dqkv, wqkv, dt), dx=dx1)
+            dx, g_n1w, g_n1b = layernorm_bwd(x, n1w.float().contiguous(), _mm(dqkv, _lp(wqkv, dt), dt), dx=dx1)
             grads[i * _PER_LAYER:(i + 1) * _PER_LAYER] = [g_n1w, g_n1b, g_wqkv.to(wqkv.dtype), g_wo.to(wo.dtype),
                                                           g_n2w, g_n2b, g_w13[:Fh].to(w1.dtype),
                                                           g_w13[Fh:].to(w3.dtype), g_w2.to(w2.dtype)]
         g_in = _wgrad(dx, fr, dt)
-        dfr = _mm(dx, w_in, dt).reshape(n, N, Ds).to(fdt)
+        dfr = _mm(dx, _lp(w_in, dt), dt).reshape(n, N, Ds).to(fdt)
         return (dfr, None, None, None, g_in.to(w_in.dtype), g_out.to(w_out.dtype), g_nw, g_nb, *grads)
 
 

@@ -303,3 +303,4 @@ def test_gather_scatter_gradients_vs_torch():
     (e3 * wg).sum().backward()
     (e4 * wg).sum().backward()
     assert torch.equal(e3, e4) and torch.equal(s3.grad, s4.grad)
+
