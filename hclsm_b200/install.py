@@ -85,9 +85,10 @@ def _ssm_block_forward(self, x):
     """SimplifiedSSMBlock.forward with softplus(dt), its clamp, the scan and
     the gate in one kernel (level0_ssm.py:58-107)."""
     from .kernels import ssm_scan
+    from .kernels.training import layer_norm
 
     residual = x
-    x = self.norm(x)
+    x = layer_norm(self.norm, x)  # this library's LayerNorm kernels, forward and backward
     z = self.in_proj(x)
     gate_pre = self.gate_proj(x)
     B_param = self.B_proj(z)

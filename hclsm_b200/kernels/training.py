@@ -27,7 +27,7 @@ from .slot_attention_kernel import _c, gru_cell, layernorm, residual_clamp, slot
 
 __all__ = ["colsum", "layernorm_bwd", "gru_cell_bwd", "slot_softmax_bwd", "residual_clamp_bwd", "relu_bwd",
            "swiglu_bwd", "event_mha_bwd", "slot_iteration_train", "level1_train", "event_gather_train",
-           "event_scatter_train"]
+           "event_scatter_train", "layer_norm"]
 
 F32 = torch.float32
 
@@ -160,6 +160,44 @@ def _mm(a, b, dt):
 def _wgrad(g, x, dt):
     """Weight gradient g^T x (out, in) in fp32."""
     return _mm(g.t(), x, dt)
+
+
+# ---- nn.LayerNorm ----------------------------------------------------------------------
+class _LayerNorm(torch.autograd.Function):
+    """nn.LayerNorm over the last dimension on this library's kernels: the
+    forward row kernel (fp32 statistics) and the backward row kernel plus
+    the deterministic two-stage column sums for the affine gradients."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, eps, out_dtype):
+        w32 = w.float().contiguous() if w is not None else None
+        b32 = b.float().contiguous() if b is not None else None
+        xs = _c(x)
+        ctx.save_for_backward(xs, w32)
+        ctx.eps, ctx.dtypes = eps, (x.dtype, None if w is None else w.dtype, None if b is None else b.dtype)
+        return layernorm(xs, w32, b32, eps, out_dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w32 = ctx.saved_tensors
+        xd, wd, bd = ctx.dtypes
+        affine = ctx.needs_input_grad[1] or ctx.needs_input_grad[2]
+        dx, dw, db = layernorm_bwd(x, w32, dy, ctx.eps, want_affine=affine)
+        return (dx.to(xd) if ctx.needs_input_grad[0] else None,
+                dw.to(wd) if (dw is not None and ctx.needs_input_grad[1]) else None,
+                db.to(bd) if (db is not None and ctx.needs_input_grad[2]) else None, None, None)
+
+
+def layer_norm(mod, x):
+    """``mod(x)`` for an nn.LayerNorm over the last dimension, on this
+    library's kernels (forward and backward).  Under CUDA autocast the output
+    is fp32, as torch runs layer_norm in fp32 there; otherwise x's dtype."""
+    _lib.require_cuda(x)
+    if tuple(mod.normalized_shape) != (x.shape[-1],):
+        raise ValueError("hclsm_b200.layer_norm normalises the last dimension only")
+    out = F32 if torch.is_autocast_enabled("cuda") else x.dtype
+    with torch.autocast("cuda", enabled=False):
+        return _LayerNorm.apply(x, mod.weight, mod.bias, float(mod.eps), out)
 
 
 # ---- slot-attention iteration ------------------------------------------------------------
