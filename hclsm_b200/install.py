@@ -131,24 +131,55 @@ def _make_dsa_forward(orig):
         attention energy and the first dormant slot are found by argmax, the
         birth projection runs for every video, and torch.where keeps it only
         where the reference would write it (energy above the threshold and a
-        dormant slot present).  No host synchronisation."""
+        dormant slot present).  No host synchronisation.  Inference in bf16
+        (no gradient recorded, d_slot a multiple of 128) runs the fused
+        refinement path with W_q folded into the keys."""
         import torch.nn.functional as F
         import torch.utils.checkpoint
 
         B, M, _ = inputs.shape
         inputs_norm = self.norm_input(inputs)
-        k = self.project_k(inputs_norm)
-        v = self.project_v(inputs_norm)
-        slots = self._init_slots(B, inputs.device)
-        for _ in range(self.n_iterations):
-            if self.use_gradient_checkpointing and self.training:
-                slots = torch.utils.checkpoint.checkpoint(self._iteration_step, slots, k, v, use_reentrant=False)
-            else:
-                slots = self._iteration_step(slots, k, v)
+        fused = (not _module_grad(self, inputs) and _work_dtype(inputs) == torch.bfloat16
+                 and self.d_slot % 128 == 0)
+        slots = None
+        if fused:
+            # inference in bf16: W_q folded into the keys, the k/v products as
+            # one GEMM, every refinement step fused (row kernels, bf16
+            # products), the final attention map from the attention core
+            from .kernels.slot_attention_kernel import (SlotIterationParams, key_value_weights, layernorm,
+                                                        project_keys_values, slot_attention_core,
+                                                        slot_attention_iterations)
+
+            key = (tuple(p._version for p in self.parameters()), "fused")
+            cache = getattr(self, "_hclsm_b200_fused", None)
+            if cache is None or cache[0] != key:
+                cache = (key, SlotIterationParams.from_module(self, torch.bfloat16),
+                         key_value_weights(self.project_k.weight, self.project_v.weight, self.project_q.weight))
+                self._hclsm_b200_fused = cache
+            p, w_kv = cache[1], cache[2]
+            k, v = project_keys_values(inputs_norm.to(torch.bfloat16).contiguous(), w_kv)
+            s0 = self._init_slots(B, inputs.device)
+            slots = slot_attention_iterations(s0, k, v, p, self.n_iterations, keys_folded=True).to(s0.dtype)
+        else:
+            k = self.project_k(inputs_norm)
+            v = self.project_v(inputs_norm)
+            slots = self._init_slots(B, inputs.device)
+            for _ in range(self.n_iterations):
+                if self.use_gradient_checkpointing and self.training:
+                    slots = torch.utils.checkpoint.checkpoint(self._iteration_step, slots, k, v,
+                                                              use_reentrant=False)
+                else:
+                    slots = self._iteration_step(slots, k, v)
         alive = torch.sigmoid(self.existence_head(slots).squeeze(-1))
         with torch.no_grad():
-            q = self.project_q(self.norm_pre_attn(slots))
-            attn = F.softmax(torch.bmm(q, k.transpose(1, 2)) * self.scale, dim=1)
+            if fused:
+                sn = layernorm(slots.reshape(-1, self.d_slot), p.ln_attn_w, p.ln_attn_b,
+                               out_dtype=torch.bfloat16).reshape(slots.shape)
+                _, attn = slot_attention_core(sn, k, v, self.scale, clamp=0.0, eps=0.0, return_attn=True,
+                                              attn_fp32=True)
+            else:
+                q = self.project_q(self.norm_pre_attn(slots))
+                attn = F.softmax(torch.bmm(q, k.transpose(1, 2)) * self.scale, dim=1)
             final_attn = attn if return_attention else None
             residual = (1.0 - attn.sum(dim=1)).abs()
             max_residual = residual.max(dim=-1).values

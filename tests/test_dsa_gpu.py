@@ -107,3 +107,34 @@ def test_no_host_sync_in_birth():
         graph.replay()
         torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_fused_bf16_inference_forward():
+    """Under bf16 autocast without gradients the patched forward runs the
+    fused path (W_q folded into the keys, stacked k/v product, fused steps,
+    attention map from the core): slots, alive and the attention map against
+    the reference's fp32 arithmetic (oracle/torch_ref.iteration_step) at 2e-2;
+    no births (threshold above any energy)."""
+    from oracle import torch_ref
+
+    torch.manual_seed(5)
+    D, N, Din, B, M = 128, 8, 96, 4, 50
+    slots0 = torch.randn(B, N, D, device="cuda")
+    mod = _DSA(D, N, 3, 0.5, 1e9, Din, slots0).cuda()
+    inputs = torch.randn(B, M, Din, device="cuda")
+    W = {n: p.detach() for n, p in mod.named_parameters()}
+    with torch.no_grad():
+        xn = mod.norm_input(inputs)
+        k, v = mod.project_k(xn), mod.project_v(xn)
+        s = slots0.clone()
+        for _ in range(3):
+            s = torch_ref.iteration_step(s, k, v, W)
+        alive_ref = torch.sigmoid(mod.existence_head(s).squeeze(-1))
+        q = mod.project_q(mod.norm_pre_attn(s))
+        attn_ref = torch.softmax(torch.bmm(q, k.transpose(1, 2)) * mod.scale, dim=1)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            slots, alive, attn = mod(inputs, return_attention=True)
+    assert mod._hclsm_b200_fused is not None  # the fused path ran
+    assert rel_err(slots.float().cpu().numpy(), s.cpu().numpy()) < 2e-2
+    assert rel_err(alive.float().cpu().numpy(), alive_ref.cpu().numpy()) < 2e-2
+    assert rel_err(attn.float().cpu().numpy(), attn_ref.cpu().numpy()) < 2e-2
