@@ -732,13 +732,20 @@ def run_slot_train(args, rank, world, dev, peaks, flush):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
-    ms = _timed(step, 10, dev, flush)
-    (ms,) = _max_over_ranks([ms], dev, world)
+    ms_eager = _timed(step, 10, dev, flush)
+    # the same step captured as one CUDA graph (the host launches one graph
+    # instead of a few hundred kernels through autograd)
+    from hclsm_b200.graphs import GraphedStep
+
+    graphed = GraphedStep(step, leaves + list(mod.parameters()), warmup=max(args.warmup, 3))
+    ms = _timed(graphed.replay, 10, dev, flush)
+    ms, ms_eager = _max_over_ranks([ms, ms_eager], dev, world)
     leg = {"metric": "slot_attention_train_frames_per_s", "value": 128 / (ms * 1e-3), "unit": "frames/s",
-           "ms_per_step": ms,
+           "ms_per_step": ms, "eager_ms_per_step": ms_eager,
            "config": "BASELINE config 2 shapes in training mode: 3 x _iteration_step forward + backward "
                      "(autograd through this library's kernels), 128 frames x 32 slots x 196 tokens x 384, bf16 "
-                     "weight products; per rank; L2 flushed between steps"}
+                     "weight products; the step captured as one CUDA graph (hclsm_b200.GraphedStep), eager "
+                     "launch time beside it; per rank; L2 flushed between steps"}
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import torch_ref
 
@@ -831,20 +838,24 @@ def run_ssm_block(args, rank, world, dev, flush):
     x.requires_grad_(True)
 
     def step():
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
             y = _ssm_block_forward(blk, x)
         y.float().sum().backward()
 
     for _ in range(max(args.warmup, 5)):
         step()
     torch.cuda.synchronize(dev)
-    ms = _timed(step, 20, dev, flush)
-    (ms,) = _max_over_ranks([ms], dev, world)
+    ms_eager = _timed(step, 20, dev, flush)
+    from hclsm_b200.graphs import GraphedStep
+
+    graphed = GraphedStep(step, [x] + list(blk.parameters()), warmup=max(args.warmup, 3))
+    ms = _timed(graphed.replay, 20, dev, flush)
+    ms, ms_eager = _max_over_ranks([ms, ms_eager], dev, world)
     return {"metric": "ssm_block_fwd_bwd_sequences_per_s", "value": x.shape[0] / (ms * 1e-3),
-            "unit": "sequences/s", "ms_per_step": ms,
+            "unit": "sequences/s", "ms_per_step": ms, "eager_ms_per_step": ms_eager,
             "config": "SimplifiedSSMBlock fwd+bwd, 256 sequences x T=64 x d_model 384 (d_inner 768, d_state 16), "
-                      "bf16 autocast, softplus(dt) fused into the scan; per rank; "
-                      "L2 flushed between steps"}
+                      "bf16 autocast, softplus(dt) fused into the scan; the step captured as one CUDA graph "
+                      "(hclsm_b200.GraphedStep), eager launch time beside it; per rank; L2 flushed between steps"}
 
 
 def main():

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 from . import _lib
 from .kernels import ssm_scan_fn  # noqa: F401
+from .graphs import GraphedStep  # noqa: F401
 
 __version__ = "0.1.0"
 
