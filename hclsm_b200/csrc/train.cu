@@ -79,43 +79,79 @@ __global__ void ln_bwd_rows_kernel(const float* __restrict__ x, const float* __r
 // Column sums over rows, first stage: block (32 columns x 8 row lanes) per
 // (column tile, row chunk); part[chunk][c].  With stats, the summand is
 // a * (x - mu_r) * rstd_r (LayerNorm's weight gradient), else a.
+// Stage 1 of the column sums: block (column tile of 32, row chunk) sums its
+// rows.  With `stats` (the LayerNorm affine gradients) it sums both dy * xhat
+// (into part) and dy (into part2, when given) in the same pass over dy.
 __global__ void colsum_part_kernel(const float* __restrict__ a, const float* __restrict__ x,
-                                   const float* __restrict__ stats, float* __restrict__ part, int64_t rows, int C,
-                                   int64_t rows_per_chunk) {
+                                   const float* __restrict__ stats, float* __restrict__ part,
+                                   float* __restrict__ part2, int64_t rows, int C, int64_t rows_per_chunk) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[8][33];
+  __shared__ float red[2][8][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
   const int chunk = blockIdx.y;
   const int64_t r0 = chunk * rows_per_chunk;
   const int64_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
-  float acc = 0.0f;
+  float acc = 0.0f, acc2 = 0.0f;
   if (c < C) {
+#pragma unroll 4
     for (int64_t r = r0 + ty; r < r1; r += 8) {
-      float v = a[r * C + c];
-      if (stats) v *= (x[r * C + c] - stats[2 * r]) * stats[2 * r + 1];
-      acc += v;
+      const float v = a[r * C + c];
+      if (stats) {
+        acc += v * ((x[r * C + c] - stats[2 * r]) * stats[2 * r + 1]);
+        acc2 += v;
+      } else {
+        acc += v;
+      }
     }
   }
-  red[ty][tx] = acc;
+  red[0][ty][tx] = acc;
+  red[1][ty][tx] = acc2;
   __syncthreads();
   if (ty == 0) {
-    float s = 0.0f;
+    float s = 0.0f, s2 = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) s += red[k][tx];
-    if (c < C) part[(int64_t)chunk * C + c] = s;
+    for (int k = 0; k < 8; ++k) {
+      s += red[0][k][tx];
+      s2 += red[1][k][tx];
+    }
+    if (c < C) {
+      part[(int64_t)chunk * C + c] = s;
+      if (part2) part2[(int64_t)chunk * C + c] = s2;
+    }
   }
 }
 
-__global__ void colsum_final_kernel(const float* __restrict__ part, float* __restrict__ out, int nchunk, int C) {
+// Stage 2: out[c] = sum over the chunks' partials, fixed order.  A block takes
+// 32 columns; its 8 warps each sum every 8th chunk (independent loads), then
+// warp 0 adds the 8 results in order.  blockIdx.y selects (part, out) or
+// (part2, out2).
+__global__ void colsum_final_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                    const float* __restrict__ part2, float* __restrict__ out2, int nchunk, int C) {
   pdl_wait();
   pdl_trigger();
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+  __shared__ float red[8][33];
+  const float* __restrict__ src = blockIdx.y ? part2 : part;
+  float* __restrict__ dst = blockIdx.y ? out2 : out;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.0f;
-  for (int k = 0; k < nchunk; ++k) s += part[(int64_t)k * C + c];
-  out[c] = s;
+  if (c < C) {
+#pragma unroll
+    for (int i = 0; i < kColChunks / 8; ++i) {
+      const int k = ty + 8 * i;
+      if (k < nchunk) s += src[(int64_t)k * C + c];
+    }
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < C) {
+    float t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][tx];
+    dst[c] = t;
+  }
 }
 
 // ---- GRUCell -----------------------------------------------------------------------
@@ -340,14 +376,20 @@ static unsigned tr_blocks(int64_t n) {
   return (unsigned)(b < 148 * 32 ? (b > 0 ? b : 1) : 148 * 32);
 }
 
-static int colsum_launch(const float* a, const float* x, const float* stats, float* part, float* out, int64_t rows,
-                         int C, cudaStream_t st) {
+// out = column sums of a (rows, C), or with stats (LayerNorm row mean / rstd)
+// the sums of a * xhat; out2 (only with stats, may be null) = the plain sums
+// of a from the same pass.  part holds kColChunks x C floats, twice that with
+// out2.
+static int colsum_launch(const float* a, const float* x, const float* stats, float* part, float* out, float* out2,
+                         int64_t rows, int C, cudaStream_t st) {
   const int nchunk = (int)(rows < kColChunks ? (rows > 0 ? rows : 1) : kColChunks);
   const int64_t per = (rows + nchunk - 1) / nchunk;
-  dim3 grid((C + 31) / 32, nchunk);
-  int rc = launch_pdl(colsum_part_kernel, grid, 256, 0, st, a, x, stats, part, rows, C, per);
+  float* p2 = (stats && out2) ? part + (size_t)kColChunks * C : nullptr;
+  int rc = launch_pdl(colsum_part_kernel, dim3((C + 31) / 32, nchunk), 256, 0, st, a, x, stats, part, p2, rows, C,
+                      per);
   if (rc != HCLSM_OK) return rc;
-  return launch_pdl(colsum_final_kernel, (unsigned)((C + 127) / 128), 128, 0, st, (const float*)part, out, nchunk, C);
+  return launch_pdl(colsum_final_kernel, dim3((C + 31) / 32, p2 ? 2 : 1), 256, 0, st, (const float*)part, out,
+                    (const float*)p2, p2 ? out2 : (float*)nullptr, nchunk, C);
 }
 
 extern "C" size_t hclsm_colsum_workspace_size(int32_t C) {
@@ -361,12 +403,12 @@ extern "C" int hclsm_colsum(const float* a, float* out, int64_t rows, int32_t C,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (rows == 0) return cudaMemsetAsync(out, 0, sizeof(float) * C, st) == cudaSuccess ? HCLSM_OK : HCLSM_ERR_LAUNCH;
   if (!workspace || workspace_bytes < hclsm_colsum_workspace_size(C)) return HCLSM_ERR_WORKSPACE;
-  return colsum_launch(a, nullptr, nullptr, static_cast<float*>(workspace), out, rows, C, st);
+  return colsum_launch(a, nullptr, nullptr, static_cast<float*>(workspace), out, nullptr, rows, C, st);
 }
 
 extern "C" size_t hclsm_layernorm_bwd_workspace_size(int64_t rows, int32_t D) {
   if (rows < 0 || D <= 0) return 0;
-  return sizeof(float) * (2 * (size_t)rows + (size_t)kColChunks * D);
+  return sizeof(float) * (2 * (size_t)rows + 2 * (size_t)kColChunks * D);
 }
 
 extern "C" int hclsm_layernorm_bwd(const float* x, const float* w, const float* dy, float* dx, float* dw, float* db,
@@ -388,11 +430,8 @@ extern "C" int hclsm_layernorm_bwd(const float* x, const float* w, const float* 
   int rc = launch_pdl(ln_bwd_rows_kernel, (unsigned)((rows + 7) / 8), 256, 0, st, x, w, dy, dx, stats, rows, D, eps,
                       accumulate);
   if (rc != HCLSM_OK) return rc;
-  if (dw) {
-    rc = colsum_launch(dy, x, stats, part, dw, rows, D, st);
-    if (rc != HCLSM_OK) return rc;
-  }
-  if (db) rc = colsum_launch(dy, nullptr, nullptr, part, db, rows, D, st);
+  if (dw) return colsum_launch(dy, x, stats, part, dw, db, rows, D, st);  // both sums in one pass
+  if (db) rc = colsum_launch(dy, nullptr, nullptr, part, db, nullptr, rows, D, st);
   return rc;
 }
 

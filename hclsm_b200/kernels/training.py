@@ -220,7 +220,7 @@ class _SlotIteration(torch.autograd.Function):
         m1 = torch._addmm_activation(b1.to(dt), mln, _lp(w1, dt).t())
         m2 = _c(_mm(m1, _lp(w2, dt).t(), dt))
         out = residual_clamp(h, m2, b2_32, 50.0)
-        ctx.save_for_backward(s2, kd, vd, sn, q, upd, gi, gh, h, mln, m1, m2, wq, w_ih, w_hh, b_ih32, b_hh32,
+        ctx.save_for_backward(s2, s_dt, kd, vd, sn, q, upd, gi, gh, h, mln, m1, m2, wq, w_ih, w_hh, b_ih32, b_hh32,
                               lna_w, lnm_w, w1, w2, b2_32)
         ctx.dt, ctx.scale, ctx.shape = dt, scale, (F_, N, D)
         ctx.in_dtypes = (slots.dtype, k.dtype, v.dtype)
@@ -228,24 +228,28 @@ class _SlotIteration(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout):
-        (s2, kd, vd, sn, q, upd, gi, gh, h, mln, m1, m2, wq, w_ih, w_hh, b_ih32, b_hh32, lna_w, lnm_w, w1, w2,
+        (s2, s_dt, kd, vd, sn, q, upd, gi, gh, h, mln, m1, m2, wq, w_ih, w_hh, b_ih32, b_hh32, lna_w, lnm_w, w1, w2,
          b2_32) = ctx.saved_tensors
         dt, scale = ctx.dt, ctx.scale
         F_, N, D = ctx.shape
         R = F_ * N
         # clamp(h + mlp + b2): residual and the MLP's output bias
         dpre = residual_clamp_bwd(h, m2, b2_32, dout.reshape(R, D), 50.0)
+        # each fp32 gradient is cast to the product dtype once, for both of
+        # its products (weight gradient and input gradient)
         db2 = colsum(dpre)
-        dW2 = _wgrad(dpre, m1, dt)
-        dm1 = relu_bwd(m1, _mm(dpre, _lp(w2, dt), dt), F32)
+        dpre_l = dpre.to(dt)
+        dW2 = _wgrad(dpre_l, m1, dt)
+        dm1 = relu_bwd(m1, _mm(dpre_l, _lp(w2, dt), dt), F32)
         db1 = colsum(dm1)
-        dW1 = _wgrad(dm1, mln, dt)
-        dmln = _mm(dm1, _lp(w1, dt), dt)
+        dm1_l = dm1.to(dt)
+        dW1 = _wgrad(dm1_l, mln, dt)
+        dmln = _mm(dm1_l, _lp(w1, dt), dt)
         dh, dlnm_w, dlnm_b = layernorm_bwd(h, lnm_w.float().contiguous(), dmln, dx=dpre.clone())
         # GRUCell
         d_gi, d_gh, ds = gru_cell_bwd(gi, gh, b_ih32, b_hh32, s2, dh)
         db_ih, db_hh = colsum(d_gi), colsum(d_gh)
-        s_dt = s2 if dt == F32 else s2.to(dt)
+        d_gi, d_gh = d_gi.to(dt), d_gh.to(dt)
         dW_ih = _wgrad(d_gi, upd.reshape(R, D), dt)
         dW_hh = _wgrad(d_gh, s_dt, dt)
         d_upd = _mm(d_gi, _lp(w_ih, dt), dt).reshape(F_, N, D)
@@ -267,7 +271,7 @@ class _SlotIteration(torch.autograd.Function):
             dv = torch.bmm(attn.transpose(1, 2), du, out_dtype=F32)
             dq = torch.bmm(d_dots, kd, out_dtype=F32)
             dk = torch.bmm(d_dots.transpose(1, 2), q, out_dtype=F32)
-        dq = dq.reshape(R, D)
+        dq = dq.reshape(R, D).to(dt)
         dWq = _wgrad(dq, sn, dt)
         dsn = _mm(dq, _lp(wq, dt), dt)
         ds, dlna_w, dlna_b = layernorm_bwd(s2, lna_w.float().contiguous(), dsn, dx=ds)
