@@ -68,7 +68,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config 0-3 legs")
-    ap.add_argument("--only", choices=["config0", "config1", "slot", "event", "block", "slot_train"],
+    ap.add_argument("--only", choices=["config0", "config1", "slot", "event", "block", "slot_train", "event_train"],
                     help="run this one leg alone (no config-4 step) and print its JSON line; for profiling")
     return ap.parse_args()
 
@@ -770,6 +770,72 @@ def run_slot_train(args, rank, world, dev, peaks, flush):
     return leg
 
 
+def run_event_train(args, rank, world, dev, flush):
+    """Config 3 in training mode: the event gather, the 3-layer Level-1 stack
+    and the scatter (hierarchy_manager.py:42-118, level1_event.py:85-133)
+    forward and backward through this library's kernels, bf16 products, into
+    the states and every Level-1 parameter.  The event compaction (which reads
+    the event count on the host) runs once before the step; the step is
+    captured as one CUDA graph, the eager launch time beside it."""
+    import torch
+
+    from hclsm_b200.graphs import GraphedStep
+    from hclsm_b200.kernels.sparse_event_attn import event_compact
+    from hclsm_b200.kernels.training import event_gather_train, event_scatter_train, level1_train
+    from hclsm_b200.workloads import Level1Module, event_inputs
+
+    e = event_inputs(seed=20, device=dev)
+    mod = Level1Module.from_weights(e["weights"], e["heads"], e["layers"], dev)
+    states = e["states"].to(torch.bfloat16).requires_grad_(True)
+    B, T, N, D = states.shape
+    idx, pos, counts, meta = event_compact(e["mask"])
+    K = max(int(meta[1].item()), 1)
+    w = torch.randn(B, T, N, D, device=dev)
+    params = [states] + list(mod.parameters())
+
+    def step():
+        for t in params:
+            t.grad = None
+        ev = event_gather_train(states, idx, pos, counts, meta, K)
+        upd = level1_train(mod, ev.reshape(B * K, N, D), None, torch.bfloat16)
+        out = event_scatter_train(states, upd.reshape(B, K, N, D), idx, pos, counts, meta, K)
+        (out.float() * w).sum().backward()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    ms_eager = _timed(step, 10, dev, flush)
+    graphed = GraphedStep(step, params, warmup=max(args.warmup, 3))
+    ms = _timed(graphed.replay, 10, dev, flush)
+    ms, ms_eager = _max_over_ranks([ms, ms_eager], dev, world)
+    n_ev = int(e["mask"].sum().item())
+    leg = {"metric": "sparse_event_attention_train_events_per_s", "value": n_ev / (ms * 1e-3),
+           "unit": "event frames/s", "ms_per_step": ms, "eager_ms_per_step": ms_eager, "event_frames": n_ev,
+           "config": "BASELINE config 3 in training mode: 8 videos x 64 steps x 32 slots x 384, Bernoulli(0.1) "
+                     "mask, gather -> 3-layer Level-1 stack -> scatter, forward + backward into the states and "
+                     "every Level-1 parameter, bf16 products; the step captured as one CUDA graph "
+                     "(hclsm_b200.GraphedStep, compaction before it); per rank; L2 flushed between steps"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import torch_ref
+
+        torch.set_num_threads(_cpu_threads())
+        ec = event_inputs(seed=20)
+        Wc = {n: t.clone().requires_grad_(True) for n, t in ec["weights"].items()}
+        wc = torch.randn(ec["states"].shape)
+
+        def cpu_step():
+            sc = ec["states"].clone().requires_grad_(True)
+            out = torch_ref.naive_sparse_event_attention(
+                sc, ec["mask"], lambda fr: torch_ref.level1_event(fr, Wc, ec["heads"], ec["layers"]))
+            (out * wc).sum().backward()
+
+        t = _best_of(cpu_step, reps=2)
+        leg["cpu_baseline"] = {"value": n_ev / t, "unit": "event frames/s", "cores": _cpu_threads(), "kind": "port",
+                               "sample": "the whole step on the host: naive_sparse_event_attention with the Level-1 "
+                                         "stack restated in PyTorch, fp32, forward + autograd backward, best of 2"}
+    return leg
+
+
 def run_event(args, rank, world, dev, peaks, flush):
     """Config 3: sparse event attention with the 3-layer Level-1 transformer
     over 8 videos x 64 steps x 32 slots x 384 (bf16), Bernoulli(0.1) mask;
@@ -908,7 +974,8 @@ def main():
                "slot": lambda: run_slot(args, rank, world, dev, peaks, flush),
                "event": lambda: run_event(args, rank, world, dev, peaks, flush),
                "block": lambda: run_ssm_block(args, rank, world, dev, flush),
-               "slot_train": lambda: run_slot_train(args, rank, world, dev, peaks, flush)}[args.only]
+               "slot_train": lambda: run_slot_train(args, rank, world, dev, peaks, flush),
+               "event_train": lambda: run_event_train(args, rank, world, dev, flush)}[args.only]
         leg = run()
         if rank == 0:
             print(json.dumps(dict(leg, n_gpus=world, leg=args.only)), flush=True)
@@ -927,6 +994,7 @@ def main():
         legs["config3_event_attention"] = run_event(args, rank, world, dev, peaks, flush)
         legs["ssm_block"] = run_ssm_block(args, rank, world, dev, flush)
         legs["config2_slot_attention_train"] = run_slot_train(args, rank, world, dev, peaks, flush)
+        legs["config3_event_attention_train"] = run_event_train(args, rank, world, dev, flush)
         del flush
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -202,3 +202,45 @@ class SlotIterModule(torch.nn.Module):
             for name, p in mod.named_parameters():
                 p.copy_(w[name])
         return mod
+
+
+class _SwiGLU(torch.nn.Module):
+    def __init__(self, d: int):
+        super().__init__()
+        self.w1 = torch.nn.Linear(d, 4 * d, bias=False)
+        self.w3 = torch.nn.Linear(d, 4 * d, bias=False)
+        self.w2 = torch.nn.Linear(4 * d, d, bias=False)
+
+
+class _EventBlock(torch.nn.Module):
+    def __init__(self, d: int, heads: int):
+        super().__init__()
+        self.norm1 = torch.nn.LayerNorm(d)
+        self.attn = torch.nn.MultiheadAttention(d, heads, bias=False, batch_first=True)
+        self.norm2 = torch.nn.LayerNorm(d)
+        self.ffn = _SwiGLU(d)
+
+
+class Level1Module(torch.nn.Module):
+    """The parameters of Level1EventDynamics (hclsm/dynamics/level1_event.py:63-83:
+    proj_in, EventTransformerBlocks with a bias-free MultiheadAttention and a
+    SwiGLU FFN, final LayerNorm, proj_out) under the same attribute names, so
+    hclsm_b200.kernels.training.level1_train runs on it without the reference
+    package; d_slot = d_model = D as in ``event_inputs``."""
+
+    def __init__(self, d: int, heads: int, layers: int):
+        super().__init__()
+        self.proj_in = torch.nn.Linear(d, d, bias=False)
+        self.proj_out = torch.nn.Linear(d, d, bias=False)
+        self.blocks = torch.nn.ModuleList([_EventBlock(d, heads) for _ in range(layers)])
+        self.norm = torch.nn.LayerNorm(d)
+
+    @classmethod
+    def from_weights(cls, w: dict, heads: int, layers: int, device="cpu"):
+        """Load ``event_inputs``' weight dict."""
+        d = w["proj_in.weight"].shape[0]
+        mod = cls(d, heads, layers).to(device)
+        with torch.no_grad():
+            for name, p in mod.named_parameters():
+                p.copy_(w[name])
+        return mod

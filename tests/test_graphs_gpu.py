@@ -85,3 +85,37 @@ def test_graphed_ssm_block_step():
     g.replay()
     torch.cuda.synchronize()
     _same(_grads(params), ref)
+
+
+def test_graphed_event_training_step():
+    """Gather -> Level-1 stack -> scatter, forward + backward, with the event
+    compaction (a host read of the event count) done before the capture."""
+    from hclsm_b200.kernels.sparse_event_attn import event_compact
+    from hclsm_b200.kernels.training import event_gather_train, event_scatter_train, level1_train
+    from hclsm_b200.workloads import Level1Module, event_inputs
+
+    dev = torch.device("cuda")
+    e = event_inputs(B=3, T=16, N=8, D=64, heads=2, layers=2, p=0.3, seed=4, device=dev)
+    mod = Level1Module.from_weights(e["weights"], e["heads"], e["layers"], dev)
+    states = e["states"].to(torch.bfloat16).requires_grad_(True)
+    B, T, N, D = states.shape
+    idx, pos, counts, meta = event_compact(e["mask"])
+    K = max(int(meta[1].item()), 1)
+    w = torch.randn(B, T, N, D, device=dev)
+    params = [states] + list(mod.parameters())
+
+    def step():
+        ev = event_gather_train(states, idx, pos, counts, meta, K)
+        upd = level1_train(mod, ev.reshape(B * K, N, D), None, torch.bfloat16)
+        out = event_scatter_train(states, upd.reshape(B, K, N, D), idx, pos, counts, meta, K)
+        (out.float() * w).sum().backward()
+
+    for p in params:
+        p.grad = None
+    step()
+    torch.cuda.synchronize()
+    ref = _grads(params)
+    g = GraphedStep(step, params)
+    g.replay()
+    torch.cuda.synchronize()
+    _same(_grads(params), ref)
