@@ -58,7 +58,8 @@ struct FwdParams {
   int64_t nseq;
   int L, D, S;
   // optional (bf16 pair kernel, d_state 9..16): h after every kStateEvery steps,
-  // (nseq, nsnap, D, 16) fp32, nsnap = ceil(L / kStateEvery) - 1
+  // (nseq, nsnap, 4, D) float4 (state quad q of channel d at [q][d]),
+  // nsnap = ceil(L / kStateEvery) - 1
   float* states;
   int softplus;  // dt is the raw projection: softplus is applied inside
 };
@@ -236,9 +237,11 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
   const int64_t wD = D / 2;  // 32-bit words per row
   const int64_t col = d0 / 2;
 
-  // state snapshots: this thread's two channels, 64 contiguous bytes each
+  // state snapshots, (nsnap, 4, D) float4 per sequence: quad q of states of
+  // channel d at [q][d], so that a warp's loads in the backward (one channel
+  // per lane) are contiguous
   const int nsnap = (L + kStateEvery - 1) / kStateEvery - 1;
-  float* snap = (p.states && act) ? p.states + ((size_t)b * nsnap * D + d0) * 16 : nullptr;
+  float4* snap = (p.states && act) ? reinterpret_cast<float4*>(p.states) + (size_t)b * nsnap * D * 4 + d0 : nullptr;
   int snap_t = kStateEvery;  // step count after which the next snapshot is taken
 
   uint32_t cx[kFwdBlk], cd[kFwdBlk], cz[kFwdBlk];
@@ -303,11 +306,12 @@ __global__ void __launch_bounds__(kFwdThreads) scan_fwd_bf16x2_kernel(FwdParams 
           if constexpr (SP == 16) {
             if (t0 + tt + 1 == snap_t) {
               if (snap_t < L && snap) {
-                float4* o = reinterpret_cast<float4*>(snap + (size_t)(snap_t / kStateEvery - 1) * D * 16);
+                float4* o = snap + (size_t)(snap_t / kStateEvery - 1) * D * 4;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                  __stcs(o + q, make_float4(h[4 * q].x, h[4 * q + 1].x, h[4 * q + 2].x, h[4 * q + 3].x));
-                  __stcs(o + 4 + q, make_float4(h[4 * q].y, h[4 * q + 1].y, h[4 * q + 2].y, h[4 * q + 3].y));
+                  __stcs(o + (size_t)q * D, make_float4(h[4 * q].x, h[4 * q + 1].x, h[4 * q + 2].x, h[4 * q + 3].x));
+                  __stcs(o + (size_t)q * D + 1,
+                         make_float4(h[4 * q].y, h[4 * q + 1].y, h[4 * q + 2].y, h[4 * q + 3].y));
                 }
               }
               snap_t += kStateEvery;
@@ -1054,10 +1058,10 @@ __global__ void __launch_bounds__(kW16Threads, 1) scan_bwd_bf16_kernel(BwdParams
         for (int q = 0; q < 8; ++q) o[q] = f2(0.0f, 0.0f);
         return;
       }
-      const float4* c = reinterpret_cast<const float4*>(p.states + (((size_t)b * (nck - 1) + (k - 1)) * D + d) * 16);
+      const float4* c = reinterpret_cast<const float4*>(p.states) + ((size_t)b * (nck - 1) + (k - 1)) * D * 4 + d;
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const float4 v = ld_hint(c + (m ^ (perm >> 2)), stream_pol);
+        const float4 v = ld_hint(c + (size_t)(m ^ (perm >> 2)) * D, stream_pol);
         o[2 * m] = f2(v.x, v.y);
         o[2 * m + 1] = f2(v.z, v.w);
       }

@@ -102,8 +102,8 @@ int hclsm_ssm_scan_bwd(const void* x, const void* dt, const float* A_log, const 
  * Scan forward that keeps state snapshots for the backward, and the backward
  * that uses them.  No counterpart in the reference (its backward,
  * ssm_scan_kernel.py:321-377, re-runs the whole forward recurrence): the
- * forward writes h after every 10 steps, (nseq, ceil(L/10) - 1, d_inner, 16)
- * fp32, and the backward starts each 10-step chunk from those snapshots
+ * forward writes h after every 10 steps, (nseq, ceil(L/10) - 1, 4, d_inner)
+ * float4 of fp32 (quad q = states 4q..4q+3 of a channel), and the backward starts each 10-step chunk from those snapshots
  * instead of sweeping the recurrence a second time.  Results are identical to
  * hclsm_ssm_scan_fwd / hclsm_ssm_scan_bwd.
  * hclsm_ssm_scan_states_size returns the snapshot bytes, or 0 where the path
